@@ -1,0 +1,445 @@
+#!/usr/bin/env python
+"""Benchmark of the exactkv hot path on B200: compressed split-K decode attention.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (the config the headline metric is quoted
+on): Llama-3.1-8B-shaped decode attention, 32 q / 8 kv heads, head dim 128,
+page 16, batch 32 x 4096 context per GPU, synthetic KV (RoPE theta 5e5, 0.04%
+zero keys, 0.3% forced raw rows; seeded, see exactkv_b200/synthetic.py). A
+step is one decode-attention call over the whole batch: the split kernel plus
+the merge kernel. Multi-GPU: one process per GPU, each with its own 32-sequence
+batch (batch sharding: no collective on the data path), weak scaling.
+
+value: compressed bytes the attention must read (algorithmic, below) x K
+steps x ranks / device time of the K steps (max over ranks), in TB/s.
+Algorithmic bytes per call, per K and V cache: 192 B per token row (sign|mantissa
+128 + codes 64) + 136 B per page (base 128 + rowmask/rowoff 8) + 256 B per raw row
+read; plus q (2 B x 128 per head) and the split partials written (fp32). The
+bf16-equivalent bytes are 2 x B x T x Hkv x 256.
+
+Timing: W warm-up steps, then K steps between two barriers + synchronize,
+timed with CUDA events on the launching stream; the cache (~425 MB) exceeds the
+126 MB L2, and a second pass with a 256 MB L2 flush between launches is
+reported as a cross-check of the per-launch kernel time. SM clocks and throttle
+reasons are sampled through NVML every 5 ms during warm-up and timing.
+
+e2e: the same metric through the public API with host buffers: each step
+copies q [B, Hq, 128] and the new token's K and V [B, Hkv, 128] from pinned
+host memory, appends them to the caches (encoding a page every 16 steps,
+with the check_overflow sync), runs decode_attention and copies the output
+back to pinned host memory; the context grows by one token per step.
+
+--impl reference: the reference algorithm on the host CPU (the numpy oracle:
+codec decode + split-K attention) over all host cores, a bounded sample per
+step (one sequence of the batch); rank 0 only.
+"""
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "compressed decode-attn µs & HBM TB/s (% of peak) at 32×4K, 32q/8kv; engine tok/s"
+UNIT = "TB/s"
+NOMINAL_HBM_GBS = 8000.0
+FALLBACK_HBM_GBS = 6650.0
+WORKLOAD = dict(workload="llama3.1-8b decode attention, compressed KV", batch_per_gpu=32, context=4096, q_heads=32,
+                kv_heads=8, head_dim=128, page=16, rope_theta=5e5, zero_keys=4e-4, forced_raw_rows=3e-3)
+PROFILE_SUMMARY = os.path.join(ROOT, "profiles", "attn_split_compressed__llama_32x4096.md")
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--batch", type=int, default=32)
+    ap.add_argument("--context", type=int, default=4096)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--num-warps", type=int, default=8)
+    return ap.parse_args()
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+def load_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profiled_traffic():
+    """dram bytes per launch of the split kernel at this workload, from the committed
+    ncu summary (line `traffic_bytes_per_launch: N`), or None."""
+    try:
+        with open(PROFILE_SUMMARY) as f:
+            for line in f:
+                if line.strip().startswith("traffic_bytes_per_launch:"):
+                    return int(float(line.split(":", 1)[1].strip().split()[0]))
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML in a thread (read-only)."""
+
+    def __init__(self, dev, interval=0.005):
+        self.samples, self.reasons, self.ok = [], set(), False
+        self.interval, self._stop = interval, threading.Event()
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(dev)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:  # noqa: BLE001 - clocks are reported as unavailable
+            self.max_mhz = None
+
+    def _names(self, bits):
+        nv, out = self.nv, []
+        table = {"sw_power_cap": getattr(nv, "nvmlClocksEventReasonSwPowerCap", 0x4),
+                 "hw_slowdown": getattr(nv, "nvmlClocksEventReasonHwSlowdown", 0x8),
+                 "sync_boost": getattr(nv, "nvmlClocksEventReasonSyncBoost", 0x10),
+                 "sw_thermal_slowdown": getattr(nv, "nvmlClocksEventReasonSwThermalSlowdown", 0x20),
+                 "hw_thermal_slowdown": getattr(nv, "nvmlClocksEventReasonHwThermalSlowdown", 0x40),
+                 "hw_power_brake_slowdown": getattr(nv, "nvmlClocksEventReasonHwPowerBrakeSlowdown", 0x80),
+                 "applications_clocks_setting": 0x2, "gpu_idle": 0x1}
+        for k, v in table.items():
+            if bits & v:
+                out.append(k)
+        return out
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                fn = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                    nv.nvmlDeviceGetCurrentClocksThrottleReasons
+                self.reasons.update(self._names(fn(self.h)))
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(self.interval)
+
+    def __enter__(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self.ok:
+            self._stop.set()
+            self.t.join()
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"]}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons - {"gpu_idle"}), "samples": len(self.samples),
+                "window": "warm-up + timed steps"}
+
+
+# ----------------------------------------------------------------------------- our arm
+
+def algorithmic_bytes(kc, vc, B, Hkv, Hq, T, ns):
+    import torch
+    npt = -(-T // 16)
+    full = T // 16
+    total = 0
+    raw_rows = 0
+    for c in (kc, vc):
+        rm = c.rowmask[:, :npt].to(torch.int64)
+        pop = torch.zeros_like(rm)
+        for bit in range(16):
+            pop += (rm >> bit) & 1
+        if npt > full:                       # the partial tail page: only rows < T are read
+            keep = (1 << (T - full * 16)) - 1
+            pop[:, full] = 0
+            tail = (rm[:, full] & keep)
+            for bit in range(16):
+                pop[:, full] += (tail >> bit) & 1
+        r = int(pop.sum().item())
+        raw_rows += r
+        total += B * npt * 16 * Hkv * 192 + B * npt * Hkv * 136 + r * 256
+    total += B * Hq * 128 * 2 + B * Hq * ns * (128 + 2) * 4
+    return total, raw_rows
+
+
+def run_ours(a, rank, world, local):
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=__import__("datetime").timedelta(seconds=120))
+
+    import exactkv_b200 as ekv
+    from exactkv_b200 import kernels, synthetic
+
+    B, T, Hq, Hkv = a.batch, a.context, 32, 8
+    TS = T + max(256, -(-(a.steps + a.warmup + 16) // 16) * 16)
+    seed = 1000 + 17 * rank
+    k = synthetic.make_kv(B, T, Hkv, seed=seed, theta=5e5, key=True, device=dev)
+    v = synthetic.make_kv(B, T, Hkv, seed=seed + 1, theta=5e5, key=False, device=dev)
+    q = synthetic.make_q(B, Hq, seed=seed + 2, device=dev)
+    kc, vc = ekv.CompressedKV(B, TS, Hkv, 128, device=dev), ekv.CompressedKV(B, TS, Hkv, 128, device=dev)
+    for b in range(B):
+        kc.prefill_slot(b, k[b:b + 1])
+        vc.prefill_slot(b, v[b:b + 1])
+    kbf = torch.zeros(B, TS, Hkv, 128, dtype=torch.bfloat16, device=dev)
+    vbf = torch.zeros_like(kbf)
+    kbf[:, :T] = k
+    vbf[:, :T] = v
+    del k, v
+    kernels.check_status(dev)
+
+    ns, sl = kernels.plan_splits(B, Hkv, T, dev)
+    stream = torch.cuda.current_stream(dev)
+    ws = kernels._workspace(dev, stream.cuda_stream, B * Hq, ns, sl)
+    out = torch.empty_like(q)
+    nbytes, raw_rows = algorithmic_bytes(kc, vc, B, Hkv, Hq, T, ns)
+    bf16_bytes = 2 * B * T * Hkv * 256
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def step(ev_a=None, ev_b=None):
+        if ev_a is not None:
+            ev_a.record(stream)
+        kernels.attention_split(q, kc, vc, T, ws, 0, ns, num_warps=a.num_warps)
+        if ev_b is not None:
+            ev_b.record(stream)
+        kernels.merge_partials(ws, B * Hq, out)
+
+    def sibling_step():
+        kernels.attention_reference(q, kbf, vbf, T, num_warps=a.num_warps)
+
+    def timed(fn, K, per_launch=False, flush_between=False):
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)] \
+            if per_launch else None
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for i in range(K):
+            if flush_between:
+                flush.zero_()
+            if per_launch:
+                fn(*evs[i])
+            else:
+                fn()
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        total = t0.elapsed_time(t1)
+        launches = [e[0].elapsed_time(e[1]) for e in evs] if per_launch else None
+        return total, launches
+
+    clocks = ClockSampler(local)
+    with clocks:
+        for _ in range(a.warmup):
+            step()
+        warm_until = time.perf_counter() + 0.3     # keep the GPU busy long enough for clock samples
+        while time.perf_counter() < warm_until:
+            step()
+        total_ms, launch_ms = timed(step, a.steps, per_launch=True)
+    kernels.check_status(dev)
+    t = torch.tensor([total_ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms = float(t.item())
+    ms_per_step = total_ms / a.steps
+    split_us = statistics.mean(launch_ms) * 1e3
+
+    _, flushed = timed(step, min(a.steps, 50), per_launch=True, flush_between=True)
+    split_us_flushed = statistics.median(flushed) * 1e3
+    for _ in range(3):
+        sibling_step()
+    sib_ms, _ = timed(sibling_step, a.steps)
+    sib_us = sib_ms / a.steps * 1e3
+
+    value = nbytes * a.steps * world / (total_ms * 1e-3) / 1e12
+    peak, peak_src = load_peak()
+    achieved_gbs = nbytes / (split_us * 1e-6) / 1e9       # all algorithmic bytes are the split kernel's
+    traffic = profiled_traffic()
+
+    e2e = None
+    if not a.no_e2e:
+        e2e = run_e2e(a, kc, vc, B, Hq, Hkv, T, dev, world, raw_rows, ns)
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        cpu = cpu_sample(T, Hkv, Hq)
+    rec = {
+        "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": round(ms_per_step, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u8 codes -> bf16 mma, fp32 softmax", "data": "synthetic",
+        "config": dict(WORKLOAD, global_batch=B * world, parallelism=f"batch-shard x{world} (independent replicas)",
+                       l2="cache 425 MB > 126 MB L2; flushed pass reported separately", splits=ns, split_len=sl,
+                       consumer_warps=a.num_warps),
+        "attn_us_per_call": round(ms_per_step * 1e3, 2),
+        "split_kernel_us": round(split_us, 2),
+        "split_kernel_us_l2_flushed": round(split_us_flushed, 2),
+        "compressed_bytes_per_call": nbytes, "raw_rows": raw_rows,
+        "raw_row_fraction": round(raw_rows / (2 * B * T * Hkv), 5),
+        "bits_per_value": round(8 * nbytes / (2 * B * T * Hkv * 128), 3),
+        "bf16_equiv_tbs": round(bf16_bytes * a.steps * world / (total_ms * 1e-3) / 1e12, 4),
+        "frac_of_nominal_8tbs": round(value / world / (NOMINAL_HBM_GBS / 1e3), 4),
+        "bf16_sibling_us_per_call": round(sib_us, 2),
+        "speedup_vs_bf16_sibling": round(sib_us / (ms_per_step * 1e3), 3),
+        "roofline": {"bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved_gbs / peak, 4), "peak_source": f"{peak_src} hbm_gbs (copy, read+write)",
+                     "traffic": traffic, "kernel": "exk::attn_split_kernel<compressed>"},
+        "gpu_launches": 2 * a.steps,
+        "clocks": clocks.summary(),
+        "e2e": e2e,
+        "cpu_baseline": cpu,
+    }
+    if rank == 0:
+        print(json.dumps(rec), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_e2e(a, kc, vc, B, Hq, Hkv, T0, dev, world, raw_rows0, ns0):
+    """Public-API decode steps with host buffers (see module docstring)."""
+    import torch
+    import torch.distributed as dist
+
+    import exactkv_b200 as ekv
+
+    K = a.steps
+    g = torch.Generator().manual_seed(77)
+    q_h = torch.randn(K, B, Hq, 128, generator=g).to(torch.bfloat16).pin_memory()
+    k_h = torch.randn(K, B, Hkv, 128, generator=g).to(torch.bfloat16).pin_memory()
+    v_h = torch.randn(K, B, Hkv, 128, generator=g).to(torch.bfloat16).pin_memory()
+    o_h = torch.empty(K, B, Hq, 128, dtype=torch.bfloat16).pin_memory()
+    stream = torch.cuda.current_stream(dev)
+    nbytes_total = 0
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(K):
+        q = q_h[i].to(dev, non_blocking=True)
+        kc.append(k_h[i].to(dev, non_blocking=True))
+        vc.append(v_h[i].to(dev, non_blocking=True))
+        if kc.T % 16 == 0:
+            ekv.check_overflow([kc, vc])
+        o = ekv.decode_attention(q, kc, vc)
+        o_h[i].copy_(o)                           # device -> host read of the step's result
+        T = kc.T
+        npt = -(-T // 16)
+        # as algorithmic_bytes(): full-page rows, page metadata, the prefill's raw rows and the
+        # raw tail rows (pages encoded during these steps add a few more raw rows, not counted)
+        nbytes_total += (2 * (B * npt * 16 * Hkv * 192 + B * npt * Hkv * 136)
+                         + (raw_rows0 + 2 * B * Hkv * (T % 16)) * 256 + B * Hq * 256 + B * Hq * ns0 * 520)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    wall = time.perf_counter() - t0
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    h2d = (B * Hq + 2 * B * Hkv) * 128 * 2
+    d2h = B * Hq * 128 * 2
+    return {"value": round(nbytes_total * world / (ms * 1e-3) / 1e12, 4), "unit": UNIT,
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms / K, 4),
+            "wall_ms_per_step": round(wall / K * 1e3, 4),
+            "what": "per step: H2D q + new K/V token (pinned), append (+page encode / check_overflow every 16), "
+                    "decode_attention, D2H output; context grows from 4096"}
+
+
+# ----------------------------------------------------------------------------- CPU (oracle) legs
+
+def _cpu_setup(T, Hkv, Hq, nseq):
+    from oracle import cpu_baseline
+    from oracle.synth import synth_kv, synth_q
+    d, per_seq = cpu_baseline.build_sample(nseq, T, Hkv, Hq, 5e5, 4242, synth_kv, synth_q)
+    pool, procs = cpu_baseline.make_pool()
+    return cpu_baseline, d, per_seq, pool, procs
+
+
+def cpu_sample(T, Hkv, Hq, seconds=10.0, nseq=4):
+    """Oracle decode + attention timed on a bounded sample: an `nseq`-sequence slice of
+    the batch (all 8 KV heads, K and V), repeated for about `seconds`, over every host core."""
+    cb, d, per_seq, pool, procs = _cpu_setup(T, Hkv, Hq, nseq)
+    seqs = list(range(nseq))
+    try:
+        cb.run_step(pool, d, seqs[:1], Hkv)             # warm the workers
+        secs = []
+        t_end = time.perf_counter() + seconds
+        while time.perf_counter() < t_end or len(secs) < 2:
+            secs.append(cb.run_step(pool, d, seqs, Hkv))
+    finally:
+        pool.close()
+        pool.join()
+    s = sum(secs)
+    return {"value": round(per_seq * nseq * len(secs) / s / 1e12, 8), "unit": UNIT, "cores": procs, "kind": "port",
+            "sample": f"{len(secs)} passes over {nseq} of the 32 sequences (4096 tokens x 8 KV heads, K and V): "
+                      f"numpy oracle decode + split-K attention, {s / len(secs) / nseq * 1e3:.1f} ms per sequence "
+                      f"with {procs} processes"}
+
+
+def run_reference(a, rank, world):
+    if rank != 0:
+        return
+    T, Hkv, Hq = a.context, 8, 32
+    cb, d, per_seq, pool, procs = _cpu_setup(T, Hkv, Hq, 1)
+    try:
+        for _ in range(max(1, a.warmup)):
+            cb.run_step(pool, d, [0], Hkv)
+        t0 = time.perf_counter()
+        for _ in range(a.steps):
+            cb.run_step(pool, d, [0], Hkv)
+        total = time.perf_counter() - t0
+    finally:
+        pool.close()
+        pool.join()
+    value = per_seq * a.steps / total / 1e12
+    sample = (f"each step: 1 sequence of the 32 x 4096 batch (8 KV heads, K and V), numpy oracle restatement "
+              f"of the reference codec decode + split-K attention over {procs} processes")
+    rec = {"metric": METRIC, "value": round(value, 8), "unit": UNIT, "n_gpus": world, "steps": a.steps,
+           "warmup": a.warmup, "ms_per_step": round(total / a.steps * 1e3, 3), "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "u8 codes -> fp32", "data": "synthetic",
+           "config": dict(WORKLOAD, global_batch=32, parallelism="host CPU"), "impl": "reference",
+           "cpu_baseline": {"value": round(value, 8), "unit": UNIT, "cores": procs, "kind": "port",
+                            "sample": sample},
+           "e2e": {"value": round(value, 8), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(rec), flush=True)
+
+
+def main():
+    a = parse_args()
+    rank, world, local = dist_env()
+    if a.impl == "reference":
+        run_reference(a, rank, world)
+        return 0
+    run_ours(a, rank, world, local)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

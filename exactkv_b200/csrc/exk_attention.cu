@@ -1,0 +1,805 @@
+// Split-K decode attention over the exponent-coded bf16 KV cache (sm_100a),
+// its uncompressed bf16 sibling, and the split merge.
+//
+// Work decomposition. A work item is one (sequence b, KV head hk, token split)
+// of the plan; persistent CTAs (one per SM) take items round-robin. Inside a
+// CTA one producer warp streams the item's 16-token pages through a 16-slot
+// shared-memory ring with TMA (cp.async.bulk.tensor, 128B/64B swizzle, no
+// multicast) and mbarriers; consumer warp w takes pages w, w+NWC, ... of the
+// item. Each consumer rebuilds K and V in registers straight into bf16 mma
+// fragments, runs the online softmax on its own pages, and at the end of the
+// item the warps' (m, l, acc) are merged through shared memory in fixed warp
+// order and written as the item's split partial.
+//
+// Tensor-core mapping ("swapped" GQA): per 16-token page the warp computes
+//   S^T[16 tok x 8 heads]  = K[16 x 128] . Q^T[128 x 8]     (8 mma, k = channels)
+//   O^T[128 ch x 8 heads] += V^T[128 x 16] . P^T[16 x 8]    (8 mma, k = tokens)
+// so the G query heads that share a KV head sit in the n=8 dimension (two
+// n-tiles for 9 <= G <= 16) and each K/V element is read once for all of them
+// (the reference packs heads into M, exactkv/kernels.py:4-8, 62-68).
+//
+// Bit-identity. The compressed and bf16 kernels instantiate the same template
+// and differ only in how a lane fills its fragment registers; the registers
+// hold the same bf16 bits in the same slots, so every mma, softmax step and
+// merge runs identically (the property exactkv/kernels.py:10-18 relies on).
+#include <cfloat>
+#include <cuda.h>
+
+#include "exk_device.cuh"
+#include "exk_host.h"
+
+namespace exk {
+
+constexpr int kRing = 16;            // pages in flight per CTA
+constexpr int kAccPitch = 132;       // floats per head row of the merge buffer (bank padding)
+constexpr uint32_t kSigma = 0x27146350u;  // mma row r (0..7) -> page token sigma(r), nibble r
+
+// Token of the page that mma row r (0..15) holds. The permutation spreads the
+// rows a quarter/half warp reads over distinct 16-byte bank groups of the
+// swizzled tiles (rows r, r+1 differ in bits 0 and 2; rows 2i cover every
+// value of bits 1-2).
+__device__ __forceinline__ int sigma(int r) { return ((kSigma >> (4 * (r & 7))) & 0xF) | (r & 8); }
+
+struct AttnArgs {
+  const uint16_t* q;            // [B, Hq, 128]
+  const int32_t* rowmask[2];    // K, V (compressed kernel only)
+  const int32_t* rowoff[2];
+  const uint16_t* raw[2];
+  int64_t raw_rows[2];
+  float* ws_o;
+  float* ws_m;
+  float* ws_l;
+  int32_t* status;
+  int B, TS, NP, Hkv, Hq, G, T;
+  int ns, split_len, s0, nsl, n_items;
+  float qk_scale;
+};
+
+// Compressed: ksm, kcode, kbase, vsm, vcode, vbase.  bf16: k, v.
+struct alignas(64) AttnMaps {
+  CUtensorMap m[6];
+};
+
+template <bool COMP, int NT, int NWC>
+struct Smem {
+  static constexpr int kSlotBytes = COMP ? 6400 : 8192;
+  static constexpr int kHeads = 8 * NT;
+  static constexpr int kRingBytes = kRing * kSlotBytes;
+  static constexpr int kAccBytes = NWC * kHeads * kAccPitch * 4;
+  static constexpr int kMLBytes = 2 * NWC * kHeads * 4;
+  static constexpr int kBarBytes = 2 * kRing * 8 + 16;
+  static constexpr int kBytes = kRingBytes + kAccBytes + kMLBytes + kBarBytes + 1024;  // + alignment slack
+  static constexpr uint32_t kTxBytes = COMP ? 2u * (2048u + 1024u + 128u) : 4u * 2048u;
+};
+
+// Shared-memory addresses of one ring slot. Compressed layout: sm tiles
+// [ring][K,V][16 rows x 128 B] (128B swizzle), code tiles [ring][K,V][16 x 64 B]
+// (64B swizzle), base rows [ring][K,V][128 B]. bf16 layout:
+// [ring][K lo, K hi, V lo, V hi][16 rows x 128 B] (128B swizzle), lo = channels 0-63.
+struct Slot {
+  uint8_t* p[6];
+};
+
+template <bool COMP>
+__device__ __forceinline__ Slot slot_ptrs(uint8_t* ring, int s) {
+  Slot o;
+  if constexpr (COMP) {
+    uint8_t* sm = ring + s * 4096;
+    uint8_t* cd = ring + kRing * 4096 + s * 2048;
+    uint8_t* bs = ring + kRing * 6144 + s * 256;
+    o.p[0] = sm; o.p[1] = cd; o.p[2] = bs;
+    o.p[3] = sm + 2048; o.p[4] = cd + 1024; o.p[5] = bs + 128;
+  } else {
+    uint8_t* b = ring + s * 8192;
+    o.p[0] = b; o.p[1] = b + 2048; o.p[2] = b + 4096; o.p[3] = b + 6144; o.p[4] = nullptr; o.p[5] = nullptr;
+  }
+  return o;
+}
+
+struct Item {
+  int b, hk, split, tok0, tok1, page0, npages;
+};
+
+__device__ __forceinline__ Item decode_item(const AttnArgs& a, int item) {
+  Item it;
+  const int bh = item / a.nsl;
+  it.split = a.s0 + item % a.nsl;
+  it.b = bh / a.Hkv;
+  it.hk = bh % a.Hkv;
+  it.tok0 = it.split * a.split_len;
+  it.tok1 = min(it.tok0 + a.split_len, a.T);
+  it.page0 = it.tok0 / kP;
+  it.npages = (it.tok1 - it.tok0 + kP - 1) / kP;
+  return it;
+}
+
+// ------------------------------------------------------------------ fragment loaders
+//
+// Lane (g = lane/4, t = lane%4).
+// K (A operand of S^T = K Q^T): rows sigma(g), sigma(g)+8; mma kk (0..7)
+//   covers channel quad 16t+4kk (kk<4) or 64+16t+4(kk-4); kw[row][2kk] holds
+//   the quad's channels 0-1, kw[row][2kk+1] channels 2-3 (bf16 pairs).
+// V (A operand of O^T = V^T P^T): token pairs (sigma(2t), sigma(2t+1)) and
+//   the same +8; m-tile mm covers channels chA = 8g+2mm (mm<4) or
+//   64+8g+2(mm-4) and chB = chA+1; vw[pair][mm][0] = (V[tokA][chA], V[tokB][chA]),
+//   vw[pair][mm][1] the same for chB.
+
+__device__ __forceinline__ void load_k_comp(const Slot& s, int g, int t, uint32_t (&kw)[2][16]) {
+  const uint8_t* sm = s.p[0];
+  const uint8_t* cd = s.p[1];
+  const uint8_t* bs = s.p[2];
+  const uint4 bl = *reinterpret_cast<const uint4*>(bs + 16 * t);
+  const uint4 bh = *reinterpret_cast<const uint4*>(bs + 64 + 16 * t);
+  const uint32_t bw[8] = {bl.x, bl.y, bl.z, bl.w, bh.x, bh.y, bh.z, bh.w};
+#pragma unroll
+  for (int rr = 0; rr < 2; ++rr) {
+    const int r = sigma(g) + 8 * rr;
+    const int sw = r & 7, cs = (r >> 1) & 3;
+    const uint4 sl = *reinterpret_cast<const uint4*>(sm + r * 128 + ((t ^ sw) << 4));
+    const uint4 sh = *reinterpret_cast<const uint4*>(sm + r * 128 + (((t + 4) ^ sw) << 4));
+    const uint4 cw = *reinterpret_cast<const uint4*>(cd + r * 64 + ((t ^ cs) << 4));
+    const uint32_t smw[8] = {sl.x, sl.y, sl.z, sl.w, sh.x, sh.y, sh.z, sh.w};
+    const uint32_t cwv[4] = {cw.x, cw.y, cw.z, cw.w};
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      const uint32_t c = kk < 4 ? lo_nibbles(cwv[kk & 3]) : hi_nibbles(cwv[kk & 3]);
+      dec4(smw[kk], c, bw[kk] & 0x7F7F7F7Fu, bw[kk], kw[rr][2 * kk], kw[rr][2 * kk + 1]);
+    }
+  }
+}
+
+__device__ __forceinline__ void load_k_bf16(const Slot& s, int g, int t, uint32_t (&kw)[2][16]) {
+#pragma unroll
+  for (int rr = 0; rr < 2; ++rr) {
+    const int r = sigma(g) + 8 * rr;
+    const int sw = r & 7;
+    const uint8_t* lo = s.p[0] + r * 128;
+    const uint8_t* hi = s.p[1] + r * 128;
+    const uint4 a = *reinterpret_cast<const uint4*>(lo + (((2 * t) ^ sw) << 4));
+    const uint4 b = *reinterpret_cast<const uint4*>(lo + (((2 * t + 1) ^ sw) << 4));
+    const uint4 c = *reinterpret_cast<const uint4*>(hi + (((2 * t) ^ sw) << 4));
+    const uint4 d = *reinterpret_cast<const uint4*>(hi + (((2 * t + 1) ^ sw) << 4));
+    const uint32_t w[16] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w, c.x, c.y, c.z, c.w, d.x, d.y, d.z, d.w};
+#pragma unroll
+    for (int i = 0; i < 16; ++i) kw[rr][i] = w[i];
+  }
+}
+
+__device__ __forceinline__ void load_v_comp(const Slot& s, int g, int t, uint32_t (&vw)[2][8][2]) {
+  const uint8_t* sm = s.p[3];
+  const uint8_t* cd = s.p[4];
+  const uint8_t* bs = s.p[5];
+  const uint2 bl = *reinterpret_cast<const uint2*>(bs + 8 * g);
+  const uint2 bh = *reinterpret_cast<const uint2*>(bs + 64 + 8 * g);
+  // base bytes duplicated per token pair: [b(c), b(c), b(c+1), b(c+1)]
+  const uint32_t eb[8] = {prmt(bl.x, bl.x, 0x1100u), prmt(bl.x, bl.x, 0x3322u), prmt(bl.y, bl.y, 0x1100u),
+                          prmt(bl.y, bl.y, 0x3322u), prmt(bh.x, bh.x, 0x1100u), prmt(bh.x, bh.x, 0x3322u),
+                          prmt(bh.y, bh.y, 0x1100u), prmt(bh.y, bh.y, 0x3322u)};
+  const int ch = g >> 1, half = (g & 1) * 8;
+#pragma unroll
+  for (int pp = 0; pp < 2; ++pp) {
+    const int ra = sigma(2 * t) + 8 * pp;
+    const int rb = sigma(2 * t + 1) + 8 * pp;
+    const uint2 al = *reinterpret_cast<const uint2*>(sm + ra * 128 + ((ch ^ (ra & 7)) << 4) + half);
+    const uint2 ah = *reinterpret_cast<const uint2*>(sm + ra * 128 + (((ch + 4) ^ (ra & 7)) << 4) + half);
+    const uint2 ac = *reinterpret_cast<const uint2*>(cd + ra * 64 + ((ch ^ ((ra >> 1) & 3)) << 4) + half);
+    const uint2 bl2 = *reinterpret_cast<const uint2*>(sm + rb * 128 + ((ch ^ (rb & 7)) << 4) + half);
+    const uint2 bh2 = *reinterpret_cast<const uint2*>(sm + rb * 128 + (((ch + 4) ^ (rb & 7)) << 4) + half);
+    const uint2 bc = *reinterpret_cast<const uint2*>(cd + rb * 64 + ((ch ^ ((rb >> 1) & 3)) << 4) + half);
+    // interleave the two tokens' bytes: [A(c), B(c), A(c+1), B(c+1)]
+    const uint32_t il[4] = {prmt(al.x, bl2.x, 0x5140u), prmt(al.x, bl2.x, 0x7362u), prmt(al.y, bl2.y, 0x5140u),
+                            prmt(al.y, bl2.y, 0x7362u)};
+    const uint32_t ih[4] = {prmt(ah.x, bh2.x, 0x5140u), prmt(ah.x, bh2.x, 0x7362u), prmt(ah.y, bh2.y, 0x5140u),
+                            prmt(ah.y, bh2.y, 0x7362u)};
+    const uint32_t jc[4] = {prmt(ac.x, bc.x, 0x5140u), prmt(ac.x, bc.x, 0x7362u), prmt(ac.y, bc.y, 0x5140u),
+                            prmt(ac.y, bc.y, 0x7362u)};
+#pragma unroll
+    for (int mm = 0; mm < 4; ++mm)
+      dec4(il[mm], lo_nibbles(jc[mm]), eb[mm] & 0x7F7F7F7Fu, eb[mm], vw[pp][mm][0], vw[pp][mm][1]);
+#pragma unroll
+    for (int mm = 4; mm < 8; ++mm)
+      dec4(ih[mm - 4], hi_nibbles(jc[mm - 4]), eb[mm] & 0x7F7F7F7Fu, eb[mm], vw[pp][mm][0], vw[pp][mm][1]);
+  }
+}
+
+__device__ __forceinline__ void load_v_bf16(const Slot& s, int g, int t, uint32_t (&vw)[2][8][2]) {
+#pragma unroll
+  for (int pp = 0; pp < 2; ++pp) {
+    const int ra = sigma(2 * t) + 8 * pp;
+    const int rb = sigma(2 * t + 1) + 8 * pp;
+    const uint4 al = *reinterpret_cast<const uint4*>(s.p[2] + ra * 128 + ((g ^ (ra & 7)) << 4));
+    const uint4 ah = *reinterpret_cast<const uint4*>(s.p[3] + ra * 128 + ((g ^ (ra & 7)) << 4));
+    const uint4 bl = *reinterpret_cast<const uint4*>(s.p[2] + rb * 128 + ((g ^ (rb & 7)) << 4));
+    const uint4 bh = *reinterpret_cast<const uint4*>(s.p[3] + rb * 128 + ((g ^ (rb & 7)) << 4));
+    const uint32_t aw[8] = {al.x, al.y, al.z, al.w, ah.x, ah.y, ah.z, ah.w};
+    const uint32_t bw[8] = {bl.x, bl.y, bl.z, bl.w, bh.x, bh.y, bh.z, bh.w};
+#pragma unroll
+    for (int mm = 0; mm < 8; ++mm) {
+      vw[pp][mm][0] = prmt(aw[mm], bw[mm], 0x5410u);
+      vw[pp][mm][1] = prmt(aw[mm], bw[mm], 0x7632u);
+    }
+  }
+}
+
+// Pool row of raw token `r` of a page, or -1 (and a status) when the
+// metadata points outside the pool.
+__device__ __forceinline__ int64_t raw_index(uint32_t rm, int32_t ro, int r, int64_t rows, int32_t* status) {
+  const int64_t idx = static_cast<int64_t>(ro) + __popc(rm & ((1u << r) - 1u));
+  if (idx < 0 || idx >= rows) {
+    set_status(status, EXK_S_RAW_INDEX);
+    return -1;
+  }
+  return idx;
+}
+
+// Rows flagged in `fl` are replaced: raw rows (bit set in rm) by their pool
+// row, rows past the valid tokens by zeros (the reference loads them as 0).
+__device__ __forceinline__ void fix_k_rows(uint32_t fl, uint32_t rm, int32_t ro, const uint16_t* raw, int64_t rows,
+                                           int32_t* status, int vr, int g, int t, uint32_t (&kw)[2][16]) {
+#pragma unroll
+  for (int rr = 0; rr < 2; ++rr) {
+    const int r = sigma(g) + 8 * rr;
+    if ((fl >> r) & 1u) {
+      uint32_t w[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) w[i] = 0u;
+      if (r < vr && raw != nullptr && ((rm >> r) & 1u)) {
+        const int64_t idx = raw_index(rm, ro, r, rows, status);
+        if (idx >= 0) {
+          const uint4* src = reinterpret_cast<const uint4*>(raw + idx * kD);
+          const uint4 a = src[2 * t], b = src[2 * t + 1], c = src[8 + 2 * t], d = src[8 + 2 * t + 1];
+          const uint32_t x[16] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w, c.x, c.y, c.z, c.w, d.x, d.y, d.z, d.w};
+#pragma unroll
+          for (int i = 0; i < 16; ++i) w[i] = x[i];
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) kw[rr][i] = w[i];
+    }
+  }
+}
+
+__device__ __forceinline__ void raw_v_words(uint32_t fl, uint32_t rm, int32_t ro, const uint16_t* raw, int64_t rows,
+                                            int32_t* status, int vr, int r, int g, uint32_t (&w)[8]) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) w[i] = 0u;
+  if (((fl >> r) & 1u) && r < vr && raw != nullptr && ((rm >> r) & 1u)) {
+    const int64_t idx = raw_index(rm, ro, r, rows, status);
+    if (idx >= 0) {
+      const uint4* src = reinterpret_cast<const uint4*>(raw + idx * kD);
+      const uint4 a = src[g], b = src[8 + g];
+      w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w; w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
+    }
+  }
+}
+
+__device__ __forceinline__ void fix_v_rows(uint32_t fl, uint32_t rm, int32_t ro, const uint16_t* raw, int64_t rows,
+                                           int32_t* status, int vr, int g, int t, uint32_t (&vw)[2][8][2]) {
+#pragma unroll
+  for (int pp = 0; pp < 2; ++pp) {
+    const int ra = sigma(2 * t) + 8 * pp;
+    const int rb = sigma(2 * t + 1) + 8 * pp;
+    const bool fa = (fl >> ra) & 1u, fb = (fl >> rb) & 1u;
+    if (fa || fb) {
+      uint32_t wa[8], wb[8];
+      raw_v_words(fl, rm, ro, raw, rows, status, vr, ra, g, wa);
+      raw_v_words(fl, rm, ro, raw, rows, status, vr, rb, g, wb);
+      const uint32_t mask = (fa ? 0x0000FFFFu : 0u) | (fb ? 0xFFFF0000u : 0u);
+#pragma unroll
+      for (int mm = 0; mm < 8; ++mm) {
+        const uint32_t n0 = prmt(wa[mm], wb[mm], 0x5410u);
+        const uint32_t n1 = prmt(wa[mm], wb[mm], 0x7632u);
+        vw[pp][mm][0] = (vw[pp][mm][0] & ~mask) | (n0 & mask);
+        vw[pp][mm][1] = (vw[pp][mm][1] & ~mask) | (n1 & mask);
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------ per-warp state
+
+template <int NT>
+struct WarpState {
+  float m[NT][2];   // running max of the lane's two heads (2t, 2t+1) per n-tile
+  float l[NT][2];   // lane-partial sum of exp2(s - m) over the lane's rows
+  float acc[NT][8][4];
+};
+
+struct PageMeta {
+  uint32_t rm[2];  // rowmask K, V
+  int32_t ro[2];   // rowoff K, V
+};
+
+template <bool COMP, int NT>
+__device__ __forceinline__ void attend_page(const Slot& s, const PageMeta& pm, int vr, const AttnArgs& a,
+                                            const uint32_t (&qf)[NT][16], WarpState<NT>& st, int g, int t) {
+  const uint32_t tailmask = vr < kP ? (0xFFFFu & ~((1u << vr) - 1u)) : 0u;
+
+  // ---- S^T = K . Q^T
+  uint32_t kw[2][16];
+  if constexpr (COMP) load_k_comp(s, g, t, kw); else load_k_bf16(s, g, t, kw);
+  {
+    const uint32_t fl = (COMP ? pm.rm[0] : 0u) | tailmask;
+    if (fl != 0u) fix_k_rows(fl, pm.rm[0], pm.ro[0], COMP ? a.raw[0] : nullptr, a.raw_rows[0], a.status, vr, g, t, kw);
+  }
+  float sc[NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk)
+      mma_bf16(sc[nt], kw[0][2 * kk], kw[1][2 * kk], kw[0][2 * kk + 1], kw[1][2 * kk + 1], qf[nt][2 * kk],
+               qf[nt][2 * kk + 1]);
+  }
+
+  // ---- V fragments (issued before the softmax so the shared loads overlap it)
+  uint32_t vw[2][8][2];
+  if constexpr (COMP) load_v_comp(s, g, t, vw); else load_v_bf16(s, g, t, vw);
+  {
+    const uint32_t fl = (COMP ? pm.rm[1] : 0u) | tailmask;
+    if (fl != 0u) fix_v_rows(fl, pm.rm[1], pm.ro[1], COMP ? a.raw[1] : nullptr, a.raw_rows[1], a.status, vr, g, t, vw);
+  }
+
+  // ---- online softmax (base 2) over the page's 16 rows
+  const int r0 = sigma(g), r1 = r0 + 8;
+  uint32_t pb[NT][2];
+  float alpha[NT][2];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    float p[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) p[i] = sc[nt][i] * a.qk_scale;
+    if (r0 >= vr) p[0] = p[1] = -INFINITY;
+    if (r1 >= vr) p[2] = p[3] = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      float mx = fmaxf(p[j], p[2 + j]);
+      mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 4));
+      mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 8));
+      mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 16));
+      const float mn = fmaxf(st.m[nt][j], mx);
+      alpha[nt][j] = ex2(st.m[nt][j] - mn);
+      p[j] = ex2(p[j] - mn);
+      p[2 + j] = ex2(p[2 + j] - mn);
+      st.l[nt][j] = st.l[nt][j] * alpha[nt][j] + p[j] + p[2 + j];
+      st.m[nt][j] = mn;
+    }
+    // P (rows = tokens, cols = heads) -> P^T fragments via 8x8 transposes
+    pb[nt][0] = movmatrix_t(pack_bf16x2(p[0], p[1]));
+    pb[nt][1] = movmatrix_t(pack_bf16x2(p[2], p[3]));
+  }
+
+  // ---- O^T = O^T * alpha + V^T . P^T
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+    for (int mm = 0; mm < 8; ++mm) {
+      float* c = st.acc[nt][mm];
+      c[0] *= alpha[nt][0];
+      c[1] *= alpha[nt][1];
+      c[2] *= alpha[nt][0];
+      c[3] *= alpha[nt][1];
+      mma_bf16(st.acc[nt][mm], vw[0][mm][0], vw[0][mm][1], vw[1][mm][0], vw[1][mm][1], pb[nt][0], pb[nt][1]);
+    }
+  }
+}
+
+template <int NT>
+__device__ __forceinline__ void load_q(const AttnArgs& a, const Item& it, int g, int t, uint32_t (&qf)[NT][16]) {
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int h = nt * 8 + g;
+    if (h < a.G) {
+      const uint4* qr =
+          reinterpret_cast<const uint4*>(a.q + (static_cast<int64_t>(it.b) * a.Hq + it.hk * a.G + h) * kD);
+      const uint4 x0 = qr[2 * t], x1 = qr[2 * t + 1], x2 = qr[8 + 2 * t], x3 = qr[8 + 2 * t + 1];
+      const uint32_t w[16] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w,
+                              x2.x, x2.y, x2.z, x2.w, x3.x, x3.y, x3.z, x3.w};
+#pragma unroll
+      for (int i = 0; i < 16; ++i) qf[nt][i] = w[i];
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) qf[nt][i] = 0u;
+    }
+  }
+}
+
+template <bool COMP>
+__device__ __forceinline__ PageMeta load_meta(const AttnArgs& a, const Item& it, int pg) {
+  PageMeta pm;
+  if constexpr (COMP) {
+    const int64_t idx = (static_cast<int64_t>(it.b) * a.NP + pg) * a.Hkv + it.hk;
+    pm.rm[0] = static_cast<uint32_t>(__ldg(a.rowmask[0] + idx)) & 0xFFFFu;
+    pm.rm[1] = static_cast<uint32_t>(__ldg(a.rowmask[1] + idx)) & 0xFFFFu;
+    pm.ro[0] = __ldg(a.rowoff[0] + idx);
+    pm.ro[1] = __ldg(a.rowoff[1] + idx);
+  } else {
+    pm.rm[0] = pm.rm[1] = 0u;
+    pm.ro[0] = pm.ro[1] = 0;
+  }
+  return pm;
+}
+
+// ------------------------------------------------------------------ kernel
+
+template <bool COMP, int NT, int NWC>
+__global__ void __launch_bounds__((NWC + 1) * 32, 1)
+    attn_split_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ AttnMaps tm) {
+  using L = Smem<COMP, NT, NWC>;
+  constexpr int H8 = L::kHeads;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* macc = reinterpret_cast<float*>(ring + L::kRingBytes);
+  float* mbuf = macc + NWC * H8 * kAccPitch;
+  float* lbuf = mbuf + NWC * H8;
+  uint64_t* full = reinterpret_cast<uint64_t*>(lbuf + NWC * H8);
+  uint64_t* empty = full + kRing;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kRing);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kRing; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == NWC) {
+    // ------------------------------------------------ TMA producer (one lane)
+    if (lane != 0) return;
+    constexpr int nmaps = COMP ? 6 : 2;
+    for (int i = 0; i < nmaps; ++i) prefetch_tmap(&tm.m[i]);
+    uint32_t gi = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; ok && item < a.n_items; item += gridDim.x) {
+      const Item it = decode_item(a, item);
+      for (int p = 0; p < it.npages; ++p, ++gi) {
+        const int slot = gi % kRing;
+        const uint32_t round = gi / kRing;
+        if (round > 0 && !mbar_wait(&empty[slot], (round - 1) & 1u)) {
+          set_status(a.status, EXK_S_EMPTY_TIMEOUT);
+          *abort_flag = 1;
+          ok = false;
+          break;
+        }
+        if (*abort_flag) {
+          ok = false;
+          break;
+        }
+        const int pg = it.page0 + p;
+        const int row = it.b * a.TS + pg * kP;
+        const Slot s = slot_ptrs<COMP>(ring, slot);
+        mbar_arrive_expect_tx(&full[slot], L::kTxBytes);
+        if constexpr (COMP) {
+          const int prow = it.b * a.NP + pg;
+          tma_load_3d(s.p[0], &tm.m[0], 0, it.hk, row, &full[slot]);
+          tma_load_3d(s.p[1], &tm.m[1], 0, it.hk, row, &full[slot]);
+          tma_load_3d(s.p[2], &tm.m[2], 0, it.hk, prow, &full[slot]);
+          tma_load_3d(s.p[3], &tm.m[3], 0, it.hk, row, &full[slot]);
+          tma_load_3d(s.p[4], &tm.m[4], 0, it.hk, row, &full[slot]);
+          tma_load_3d(s.p[5], &tm.m[5], 0, it.hk, prow, &full[slot]);
+        } else {
+          tma_load_3d(s.p[0], &tm.m[0], 0, it.hk, row, &full[slot]);
+          tma_load_3d(s.p[1], &tm.m[0], 64, it.hk, row, &full[slot]);
+          tma_load_3d(s.p[2], &tm.m[1], 0, it.hk, row, &full[slot]);
+          tma_load_3d(s.p[3], &tm.m[1], 64, it.hk, row, &full[slot]);
+        }
+      }
+    }
+    // Every copy this lane issued lands before the CTA may exit.
+    for (uint32_t i = gi > kRing ? gi - kRing : 0; i < gi; ++i) {
+      if (!mbar_wait(&full[i % kRing], (i / kRing) & 1u)) {
+        set_status(a.status, EXK_S_DRAIN_TIMEOUT);
+        break;
+      }
+    }
+    return;
+  }
+
+  // -------------------------------------------------- consumers
+  const int g = lane >> 2, t = lane & 3;
+  const int ctid = threadIdx.x;  // 0 .. NWC*32-1
+  uint32_t gbase = 0;
+  bool aborted = false;
+  WarpState<NT> st;
+  uint32_t qf[NT][16];
+
+  for (int item = blockIdx.x; item < a.n_items; item += gridDim.x) {
+    const Item it = decode_item(a, item);
+    load_q<NT>(a, it, g, t, qf);
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      st.m[nt][0] = st.m[nt][1] = -INFINITY;
+      st.l[nt][0] = st.l[nt][1] = 0.f;
+#pragma unroll
+      for (int mm = 0; mm < 8; ++mm) st.acc[nt][mm][0] = st.acc[nt][mm][1] = st.acc[nt][mm][2] = st.acc[nt][mm][3] = 0.f;
+    }
+    PageMeta pm_next;
+    if (warp < it.npages) pm_next = load_meta<COMP>(a, it, it.page0 + warp);
+    for (int p = warp; p < it.npages; p += NWC) {
+      const PageMeta pm = pm_next;
+      if (p + NWC < it.npages) pm_next = load_meta<COMP>(a, it, it.page0 + p + NWC);
+      const uint32_t gidx = gbase + p;
+      const int slot = gidx % kRing;
+      if (!aborted) {
+        if (*abort_flag) {
+          aborted = true;
+        } else if (!mbar_wait(&full[slot], (gidx / kRing) & 1u)) {
+          set_status(a.status, EXK_S_FULL_TIMEOUT);
+          *abort_flag = 1;
+          aborted = true;
+        }
+      }
+      if (!aborted) {
+        const int vr = min(kP, it.tok1 - (it.page0 + p) * kP);
+        attend_page<COMP, NT>(slot_ptrs<COMP>(ring, slot), pm, vr, a, qf, st, g, t);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+      }
+    }
+    gbase += it.npages;
+
+    // ---- merge the consumer warps' states (fixed warp order) and write the split partial
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        float l = st.l[nt][j];
+        l += __shfl_xor_sync(0xFFFFFFFFu, l, 4);
+        l += __shfl_xor_sync(0xFFFFFFFFu, l, 8);
+        l += __shfl_xor_sync(0xFFFFFFFFu, l, 16);
+        st.l[nt][j] = l;
+      }
+    named_barrier(1, NWC * 32);
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const int h0 = nt * 8 + 2 * t;
+      if (g == 0) {
+        mbuf[warp * H8 + h0] = st.m[nt][0];
+        mbuf[warp * H8 + h0 + 1] = st.m[nt][1];
+        lbuf[warp * H8 + h0] = st.l[nt][0];
+        lbuf[warp * H8 + h0 + 1] = st.l[nt][1];
+      }
+#pragma unroll
+      for (int mm = 0; mm < 8; ++mm) {
+        const int chA = mm < 4 ? 8 * g + 2 * mm : 64 + 8 * g + 2 * (mm - 4);
+        float* r = macc + (warp * H8 + h0) * kAccPitch + chA;
+        *reinterpret_cast<float2*>(r) = make_float2(st.acc[nt][mm][0], st.acc[nt][mm][2]);
+        *reinterpret_cast<float2*>(r + kAccPitch) = make_float2(st.acc[nt][mm][1], st.acc[nt][mm][3]);
+      }
+    }
+    named_barrier(1, NWC * 32);
+    for (int e = ctid; e < H8 * 32; e += NWC * 32) {
+      const int h = e >> 5, c4 = (e & 31) * 4;
+      if (h >= a.G) continue;
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < NWC; ++w) M = fmaxf(M, mbuf[w * H8 + h]);
+      float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+      float lsum = 0.f;
+#pragma unroll
+      for (int w = 0; w < NWC; ++w) {
+        const float mw = mbuf[w * H8 + h];
+        const float sc = mw == -INFINITY ? 0.f : ex2(mw - M);
+        const float4 v = *reinterpret_cast<const float4*>(macc + (w * H8 + h) * kAccPitch + c4);
+        o.x += sc * v.x;
+        o.y += sc * v.y;
+        o.z += sc * v.z;
+        o.w += sc * v.w;
+        lsum += sc * lbuf[w * H8 + h];
+      }
+      const int64_t row = static_cast<int64_t>(it.b) * a.Hq + it.hk * a.G + h;
+      const int64_t col = row * a.ns + it.split;
+      *reinterpret_cast<float4*>(a.ws_o + col * kD + c4) = o;
+      if (c4 == 0) {
+        a.ws_m[col] = M;
+        a.ws_l[col] = lsum;
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------ merge
+
+__global__ void __launch_bounds__(128) merge_kernel(const float* __restrict__ o, const float* __restrict__ m,
+                                                    const float* __restrict__ l, int ns, int rows,
+                                                    uint16_t* __restrict__ out) {
+  const int row = blockIdx.x * 4 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float* mr = m + static_cast<int64_t>(row) * ns;
+  const float* lr = l + static_cast<int64_t>(row) * ns;
+  float M = -INFINITY;
+  for (int s = 0; s < ns; ++s) M = fmaxf(M, mr[s]);
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float den = 0.f;
+  for (int s = 0; s < ns; ++s) {
+    const float w = ex2(mr[s] - M);
+    const float4 v = reinterpret_cast<const float4*>(o + (static_cast<int64_t>(row) * ns + s) * kD)[lane];
+    acc.x += w * v.x;
+    acc.y += w * v.y;
+    acc.z += w * v.z;
+    acc.w += w * v.w;
+    den += w * lr[s];
+  }
+  uint2 r;
+  r.x = pack_bf16x2(acc.x / den, acc.y / den);
+  r.y = pack_bf16x2(acc.z / den, acc.w / den);
+  reinterpret_cast<uint2*>(out + static_cast<int64_t>(row) * kD)[lane] = r;
+}
+
+// ------------------------------------------------------------------ host side
+
+namespace {
+
+template <bool COMP, int NT, int NWC>
+int launch_split(const AttnArgs& a, const AttnMaps& maps, int grid, int device, cudaStream_t stream) {
+  using L = Smem<COMP, NT, NWC>;
+  static bool configured[64] = {};
+  auto kern = attn_split_kernel<COMP, NT, NWC>;
+  if (!configured[device]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    configured[device] = true;
+  }
+  kern<<<grid, (NWC + 1) * 32, L::kBytes, stream>>>(a, maps);
+  return launch_status();
+}
+
+template <bool COMP>
+int dispatch_split(const AttnArgs& a, const AttnMaps& maps, int grid, int nwc, int device, cudaStream_t stream) {
+  const bool two = a.G > 8;
+  if (nwc == 4) return two ? launch_split<COMP, 2, 4>(a, maps, grid, device, stream)
+                           : launch_split<COMP, 1, 4>(a, maps, grid, device, stream);
+  return two ? launch_split<COMP, 2, 8>(a, maps, grid, device, stream)
+             : launch_split<COMP, 1, 8>(a, maps, grid, device, stream);
+}
+
+// Validates the shapes shared by both split kernels and fills AttnArgs.
+int common_args(AttnArgs& a, const uint16_t* q, int B, int TS, int Hkv, int Hq, int T, int s0, int s1,
+                const exk_partials* ws, int nwc, float qk_scale, int32_t* status) {
+  if (ws == nullptr || q == nullptr) return EXK_EARG;
+  if (B <= 0 || Hkv <= 0 || Hq <= 0 || T <= 0 || TS <= 0 || TS % kP != 0 || T > TS) return EXK_EARG;
+  if (Hq % Hkv != 0) return EXK_EARG;
+  if (Hq / Hkv > 16) return EXK_EHEADS;
+  if (nwc != 4 && nwc != 8) return EXK_EARG;
+  if (ws->ns <= 0 || ws->split_len <= 0 || ws->split_len % kP != 0) return EXK_EARG;
+  if (static_cast<int64_t>(ws->ns) * ws->split_len < T) return EXK_EARG;
+  if (s0 < 0 || s1 > ws->ns || s0 >= s1) return EXK_EARG;
+  if (static_cast<int64_t>(s0) * ws->split_len >= T) return EXK_EARG;
+  if (!aligned16(q) || !aligned16(ws->o)) return EXK_EALIGN;
+  if (static_cast<int64_t>(B) * TS * Hkv > (int64_t{1} << 31) - 1) return EXK_EARG;
+  a.q = q;
+  a.ws_o = ws->o;
+  a.ws_m = ws->m;
+  a.ws_l = ws->l;
+  a.status = status;
+  a.B = B;
+  a.TS = TS;
+  a.NP = TS / kP;
+  a.Hkv = Hkv;
+  a.Hq = Hq;
+  a.G = Hq / Hkv;
+  a.T = T;
+  a.ns = ws->ns;
+  a.split_len = ws->split_len;
+  a.s0 = s0;
+  // splits entirely past T (possible when s1 > the plan's last split) hold no work
+  const int last = (T - 1) / ws->split_len;
+  a.nsl = min(s1, last + 1) - s0;
+  const int64_t items = static_cast<int64_t>(B) * Hkv * a.nsl;
+  if (items > (int64_t{1} << 30)) return EXK_EARG;
+  a.n_items = static_cast<int>(items);
+  a.qk_scale = qk_scale;
+  for (int i = 0; i < 2; ++i) {
+    a.rowmask[i] = nullptr;
+    a.rowoff[i] = nullptr;
+    a.raw[i] = nullptr;
+    a.raw_rows[i] = 0;
+  }
+  return 0;
+}
+
+}  // namespace
+
+}  // namespace exk
+
+using namespace exk;
+
+extern "C" int exk_plan_splits(int B, int Hkv, int T, int num_ctas, int32_t* ns_out, int32_t* sl_out) {
+  if (B <= 0 || Hkv <= 0 || T <= 0 || num_ctas <= 0 || ns_out == nullptr || sl_out == nullptr) return EXK_EARG;
+  // Cost of a candidate = (items on the busiest CTA) x (pages per item + fixed
+  // per-item overhead of ~2 pages: Q load, pipeline refill, epilogue merge).
+  const int64_t npt = (T + kP - 1) / kP;
+  const int64_t bh = static_cast<int64_t>(B) * Hkv;
+  constexpr int64_t kItemOverheadPages = 2;
+  const int64_t nmax = std::min<int64_t>(npt, std::max<int64_t>(1, 8 * static_cast<int64_t>(num_ctas)));
+  int64_t best_cost = -1, best_spp = npt;
+  int64_t prev_spp = -1;
+  for (int64_t n = 1; n <= nmax; ++n) {
+    const int64_t spp = (npt + n - 1) / n;
+    if (spp == prev_spp) continue;
+    prev_spp = spp;
+    const int64_t nsr = (npt + spp - 1) / spp;
+    if (nsr > 4096) break;
+    const int64_t items = bh * nsr;
+    const int64_t waves = (items + num_ctas - 1) / num_ctas;
+    const int64_t cost = waves * (spp + kItemOverheadPages);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best_spp = spp;
+    }
+  }
+  *sl_out = static_cast<int32_t>(best_spp * kP);
+  *ns_out = static_cast<int32_t>((npt + best_spp - 1) / best_spp);
+  return 0;
+}
+
+extern "C" int exk_attn_split_compressed(const uint16_t* q, const exk_cview* k, const exk_cview* v, int B, int TS,
+                                         int Hkv, int Hq, int T, int s0, int s1, const exk_partials* ws,
+                                         int consumer_warps, float qk_scale, int32_t* status, int device,
+                                         void* stream) {
+  if (k == nullptr || v == nullptr) return EXK_EARG;
+  AttnArgs a;
+  int r = common_args(a, q, B, TS, Hkv, Hq, T, s0, s1, ws, consumer_warps, qk_scale, status);
+  if (r != 0) return r;
+  int sms = 0;
+  if ((r = use_device(device, &sms)) != 0) return r;
+  const exk_cview* cv[2] = {k, v};
+  AttnMaps maps;
+  for (int i = 0; i < 2; ++i) {
+    const exk_cview* c = cv[i];
+    if (!aligned16(c->sm) || !aligned16(c->code) || !aligned16(c->base) || !aligned16(c->raw)) return EXK_EALIGN;
+    if (c->rowmask == nullptr || c->rowoff == nullptr || c->raw_rows <= 0) return EXK_EARG;
+    a.rowmask[i] = c->rowmask;
+    a.rowoff[i] = c->rowoff;
+    a.raw[i] = c->raw;
+    a.raw_rows[i] = c->raw_rows;
+    const uint64_t rows = static_cast<uint64_t>(B) * TS, prows = static_cast<uint64_t>(B) * (TS / kP);
+    if ((r = make_tmap_3d(&maps.m[3 * i + 0], CU_TENSOR_MAP_DATA_TYPE_UINT8, c->sm, 128, Hkv, rows, 128,
+                          128ull * Hkv, 128, 1, kP, CU_TENSOR_MAP_SWIZZLE_128B)) != 0)
+      return r;
+    if ((r = make_tmap_3d(&maps.m[3 * i + 1], CU_TENSOR_MAP_DATA_TYPE_UINT8, c->code, 64, Hkv, rows, 64,
+                          64ull * Hkv, 64, 1, kP, CU_TENSOR_MAP_SWIZZLE_64B)) != 0)
+      return r;
+    if ((r = make_tmap_3d(&maps.m[3 * i + 2], CU_TENSOR_MAP_DATA_TYPE_UINT8, c->base, 128, Hkv, prows, 128,
+                          128ull * Hkv, 128, 1, 1, CU_TENSOR_MAP_SWIZZLE_NONE)) != 0)
+      return r;
+  }
+  const int grid = static_cast<int>(std::min<int64_t>(a.n_items, sms));
+  return dispatch_split<true>(a, maps, grid, consumer_warps, device, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int exk_attn_split_bf16(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int TS, int Hkv,
+                                   int Hq, int T, int s0, int s1, const exk_partials* ws, int consumer_warps,
+                                   float qk_scale, int32_t* status, int device, void* stream) {
+  if (k == nullptr || v == nullptr) return EXK_EARG;
+  AttnArgs a;
+  int r = common_args(a, q, B, TS, Hkv, Hq, T, s0, s1, ws, consumer_warps, qk_scale, status);
+  if (r != 0) return r;
+  int sms = 0;
+  if ((r = use_device(device, &sms)) != 0) return r;
+  if (!aligned16(k) || !aligned16(v)) return EXK_EALIGN;
+  AttnMaps maps;
+  const uint64_t rows = static_cast<uint64_t>(B) * TS;
+  if ((r = make_tmap_3d(&maps.m[0], CU_TENSOR_MAP_DATA_TYPE_UINT16, k, 128, Hkv, rows, 256, 256ull * Hkv, 64, 1, kP,
+                        CU_TENSOR_MAP_SWIZZLE_128B)) != 0)
+    return r;
+  if ((r = make_tmap_3d(&maps.m[1], CU_TENSOR_MAP_DATA_TYPE_UINT16, v, 128, Hkv, rows, 256, 256ull * Hkv, 64, 1, kP,
+                        CU_TENSOR_MAP_SWIZZLE_128B)) != 0)
+    return r;
+  const int grid = static_cast<int>(std::min<int64_t>(a.n_items, sms));
+  return dispatch_split<false>(a, maps, grid, consumer_warps, device, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int exk_attn_merge(const exk_partials* ws, int rows, uint16_t* out, int device, void* stream) {
+  if (ws == nullptr || out == nullptr || rows <= 0 || ws->ns <= 0) return EXK_EARG;
+  if (!aligned16(ws->o) || (reinterpret_cast<uintptr_t>(out) & 7u) != 0) return EXK_EALIGN;
+  int r = use_device(device, nullptr);
+  if (r != 0) return r;
+  merge_kernel<<<(rows + 3) / 4, 128, 0, static_cast<cudaStream_t>(stream)>>>(ws->o, ws->m, ws->l, ws->ns, rows, out);
+  return launch_status();
+}

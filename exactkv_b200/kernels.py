@@ -1,0 +1,244 @@
+"""Drop-in replacement of the reference's exactkv/kernels.py, backed by the
+sm_100a kernels of libexactkv_b200.so through its C ABI.
+
+Same public names and argument meanings as the reference module
+(exactkv/kernels.py:273-346): P, LOG2E, choose_split, attention_compressed,
+attention_reference, decode_to_bf16, encode_pages. Everything runs on the
+caller's current CUDA stream and nothing synchronises the host, except
+check_status(). There is no CPU or Triton fallback: without the library this
+module fails to import.
+
+Differences from the reference, all invisible to callers of the reference API:
+  * the split layout comes from plan_splits() (persistent CTAs over the SMs)
+    instead of choose_split(); choose_split() is kept for compatibility;
+  * BLOCK_N and num_stages are accepted and ignored (pages are 16 tokens and
+    the TMA ring depth is fixed); num_warps selects 4 or 8 consumer warps
+    (default 8) — the compressed and bf16 kernels called with the same value
+    stay bit-identical, as in the reference;
+  * the page encoder assigns raw-pool slots in (sequence, page, head) order,
+    so rowoff/raw match encode_reference byte for byte as well.
+"""
+import ctypes
+
+import torch
+
+from ._lib import CView, Partials, check, lib
+
+LOG2E = 1.4426950408889634
+P = 16          # tokens per page
+D = 128         # head dimension
+
+_I32 = ctypes.c_int32
+
+
+def choose_split(B, Hkv, T, BLOCK_N, target=512):
+    """The reference's split rule (exactkv/kernels.py:273-277): at most `target`
+    programs, split length a multiple of BLOCK_N. Returns (splits, split length)."""
+    def cdiv(a, b):
+        return (a + b - 1) // b
+
+    ns = max(1, min(cdiv(T, BLOCK_N), target // max(1, B * Hkv)))
+    split_len = cdiv(cdiv(T, ns), BLOCK_N) * BLOCK_N
+    return cdiv(T, split_len), split_len
+
+
+_SMS = {}
+
+
+def num_sms(device=None):
+    """SM count of a CUDA device (the number of persistent attention CTAs)."""
+    dev = _device_index(device)
+    if dev not in _SMS:
+        n = lib.exk_num_sms(dev)
+        if n <= 0:
+            check(n if n < 0 else -1, "exk_num_sms")
+        _SMS[dev] = n
+    return _SMS[dev]
+
+
+def plan_splits(B, Hkv, T, device=None, num_ctas=None):
+    """(splits, split length in tokens) of the attention plan."""
+    ns, sl = _I32(), _I32()
+    ctas = num_ctas if num_ctas is not None else num_sms(device)
+    check(lib.exk_plan_splits(B, Hkv, T, ctas, ctypes.byref(ns), ctypes.byref(sl)), "exk_plan_splits")
+    return ns.value, sl.value
+
+
+def _device_index(device):
+    if device is None:
+        return torch.cuda.current_device()
+    if isinstance(device, int):
+        return device
+    device = torch.device(device)
+    return device.index if device.index is not None else torch.cuda.current_device()
+
+
+# ----------------------------------------------------------------------------- status word and scratch
+
+_STATUS = {}   # device index -> int32[1] status word written by the kernels
+_CHAIN = {}    # (device, stream) -> int32[2] encoder chain state for callers without their own
+
+
+def status_tensor(device):
+    dev = _device_index(device)
+    t = _STATUS.get(dev)
+    if t is None:
+        t = _STATUS[dev] = torch.zeros(1, dtype=torch.int32, device=f"cuda:{dev}")
+    return t
+
+
+def check_status(device=None, reset=True):
+    """Synchronises with the device and raises RuntimeError if a kernel recorded a
+    fault (a timed-out wait or an out-of-range raw index) since the last check."""
+    t = status_tensor(device)
+    code = int(t.item())
+    if code != 0:
+        if reset:
+            t.zero_()
+        raise RuntimeError(f"exactkv_b200 device status {code}: {lib.exk_status_string(code).decode()}")
+    return 0
+
+
+def _chain_tensor(device, stream):
+    key = (_device_index(device), stream)
+    t = _CHAIN.get(key)
+    if t is None:
+        t = _CHAIN[key] = torch.zeros(2, dtype=torch.int32, device=device)
+    return t
+
+
+# ----------------------------------------------------------------------------- split workspaces
+
+_WS = {}  # (device, stream, rows, ns) -> (o, m, l, Partials); reused by calls on the same stream
+
+
+def _workspace(device, stream, rows, ns, split_len):
+    key = (device.index, stream, rows, ns)
+    ws = _WS.get(key)
+    if ws is None:
+        f32 = dict(device=device, dtype=torch.float32)
+        o, m, l = torch.empty(rows, ns, D, **f32), torch.empty(rows, ns, **f32), torch.empty(rows, ns, **f32)
+        ws = _WS[key] = (o, m, l, Partials(o.data_ptr(), m.data_ptr(), l.data_ptr(), ns, split_len))
+    ws[3].split_len = split_len
+    return ws
+
+
+def _consumer_warps(num_warps):
+    return 4 if num_warps is not None and num_warps <= 4 else 8
+
+
+def _view_from_dict(c):
+    raw = c["raw"]
+    cv = CView(c["sm"].data_ptr(), c["code"].data_ptr(), c["base"].data_ptr(), c["rowmask"].data_ptr(),
+               c["rowoff"].data_ptr(), raw.data_ptr(), raw.shape[0])
+    return cv, c["shape"][1], c["shape"][2]
+
+
+def _cache_args(c):
+    """(exk_cview, TS, Hkv) from a CompressedKV (cached there) or from its .buffers() dict."""
+    if isinstance(c, dict):
+        return _view_from_dict(c)
+    return c.kernel_view(), c.TS, c.H
+
+
+def _check_q(q, T, TS):
+    if q.dim() != 3 or q.shape[2] != D or q.dtype != torch.bfloat16 or not q.is_contiguous() or not q.is_cuda:
+        raise ValueError("q must be a contiguous CUDA bf16 tensor [B, Hq, 128]")
+    if not 0 < T <= TS:
+        raise ValueError(f"T={T} out of range (1..{TS})")
+
+
+def attention_split(q, kc, vc, T, ws, s0, s1, num_warps=None):
+    """Split partials of the compressed attention for splits [s0, s1) of ws's plan
+    (the per-GPU step of a KV-sequence split). ws: (o, m, l, Partials)."""
+    ka, TS, Hkv = _cache_args(kc)
+    va, _, _ = _cache_args(vc)
+    _check_q(q, T, TS)
+    B, Hq, _ = q.shape
+    dev = q.device.index
+    stream = torch.cuda.current_stream(q.device).cuda_stream
+    rc = lib.exk_attn_split_compressed(q.data_ptr(), ctypes.byref(ka), ctypes.byref(va), B, TS, Hkv, Hq, T, s0, s1,
+                                       ctypes.byref(ws[3]), _consumer_warps(num_warps), D ** -0.5 * LOG2E,
+                                       status_tensor(dev).data_ptr(), dev, stream)
+    check(rc, "exk_attn_split_compressed")
+
+
+def merge_partials(ws, rows, out):
+    stream = torch.cuda.current_stream(out.device).cuda_stream
+    check(lib.exk_attn_merge(ctypes.byref(ws[3]), rows, out.data_ptr(), out.device.index, stream), "exk_attn_merge")
+    return out
+
+
+def attention_compressed(q, kc, vc, T, BLOCK_N=64, num_warps=None, num_stages=1):
+    """q [B, Hq, D] bf16 contiguous; kc, vc: CompressedKV objects (or their .buffers()
+    dicts); T: valid tokens. Returns bf16 [B, Hq, D]. Bit-identical to
+    attention_reference called with the same num_warps."""
+    ka, TS, Hkv = _cache_args(kc)
+    va, _, _ = _cache_args(vc)
+    _check_q(q, T, TS)
+    B, Hq, _ = q.shape
+    dev = q.device.index
+    stream = torch.cuda.current_stream(q.device).cuda_stream
+    ns, sl = plan_splits(B, Hkv, T, dev)
+    ws = _workspace(q.device, stream, B * Hq, ns, sl)
+    rc = lib.exk_attn_split_compressed(q.data_ptr(), ctypes.byref(ka), ctypes.byref(va), B, TS, Hkv, Hq, T, 0, ns,
+                                       ctypes.byref(ws[3]), _consumer_warps(num_warps), D ** -0.5 * LOG2E,
+                                       status_tensor(dev).data_ptr(), dev, stream)
+    check(rc, "exk_attn_split_compressed")
+    out = torch.empty_like(q)
+    check(lib.exk_attn_merge(ctypes.byref(ws[3]), B * Hq, out.data_ptr(), dev, stream), "exk_attn_merge")
+    return out
+
+
+def attention_reference(q, k, v, T, BLOCK_N=64, num_warps=None, num_stages=1):
+    """The same computation on uncompressed bf16 K, V of shape [B, TS, Hkv, D] (contiguous)."""
+    if k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16 or not (k.is_contiguous() and v.is_contiguous()):
+        raise ValueError("k and v must be contiguous bf16 [B, TS, Hkv, 128]")
+    TS, Hkv = k.shape[1], k.shape[2]
+    _check_q(q, T, TS)
+    B, Hq, _ = q.shape
+    dev = q.device.index
+    stream = torch.cuda.current_stream(q.device).cuda_stream
+    ns, sl = plan_splits(B, Hkv, T, dev)
+    ws = _workspace(q.device, stream, B * Hq, ns, sl)
+    rc = lib.exk_attn_split_bf16(q.data_ptr(), k.data_ptr(), v.data_ptr(), B, TS, Hkv, Hq, T, 0, ns,
+                                 ctypes.byref(ws[3]), _consumer_warps(num_warps), D ** -0.5 * LOG2E,
+                                 status_tensor(dev).data_ptr(), dev, stream)
+    check(rc, "exk_attn_split_bf16")
+    out = torch.empty_like(q)
+    check(lib.exk_attn_merge(ctypes.byref(ws[3]), B * Hq, out.data_ptr(), dev, stream), "exk_attn_merge")
+    return out
+
+
+def decode_to_bf16(c, T):
+    """Compressed buffers (a .buffers() dict) -> bf16 [B, T, H, D] through the same
+    decoder the attention kernel uses."""
+    cv, TS, H = _view_from_dict(c)
+    B = c["shape"][0]
+    dev = c["sm"].device
+    out = torch.empty(B, T, H, D, dtype=torch.bfloat16, device=dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    check(lib.exk_decode_to_bf16(ctypes.byref(cv), B, TS, H, T, out.data_ptr(),
+                                 status_tensor(dev.index).data_ptr(), dev.index, stream), "exk_decode_to_bf16")
+    return out
+
+
+def encode_pages(src, strides, buf, b0, pg0, nb, npg):
+    """Encode nb sequences x npg pages. src points at sequence b0's first page to
+    encode; strides = (seq, page, token, head) in elements. buf: dict with sm, code,
+    base, rowmask, rowoff, raw, cnt, cap, TS, H, D (and optionally `chain`, the
+    encoder's 2-word scratch; a per-stream one is used otherwise)."""
+    if buf["D"] != D or src.dtype != torch.bfloat16 or src.stride(-1) != 1:
+        raise ValueError("src must be bf16 with contiguous channels; D = 128 only")
+    dev = src.device
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    chain = buf.get("chain")
+    if chain is None:
+        chain = _chain_tensor(dev, stream)
+    s_b, s_pg, s_p, s_h = (int(s) for s in strides)
+    rc = lib.exk_encode_pages(src.data_ptr(), s_b, s_pg, s_p, s_h, buf["sm"].data_ptr(), buf["code"].data_ptr(),
+                              buf["base"].data_ptr(), buf["rowmask"].data_ptr(), buf["rowoff"].data_ptr(),
+                              buf["raw"].data_ptr(), int(buf["cap"]), buf["cnt"].data_ptr(), chain.data_ptr(),
+                              b0, pg0, nb, npg, buf["H"], buf["TS"], status_tensor(dev.index).data_ptr(),
+                              dev.index, stream)
+    check(rc, "exk_encode_pages")

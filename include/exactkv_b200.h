@@ -1,0 +1,139 @@
+/*
+ * exactkv_b200 — C ABI of the B200 (sm_100a) kernels for the exactkv hot path.
+ *
+ * The library (exactkv_b200/libexactkv_b200.so) replaces the Triton module
+ * exactkv/kernels.py of the reference. Every entry point takes plain device
+ * pointers, element counts and strides, the CUDA device index and a
+ * cudaStream_t passed as `void *`. Nothing here allocates device memory: the
+ * caller owns every buffer, including the split-K workspace and the 2-word
+ * encoder chain state. Work is enqueued on `stream` and nothing synchronises.
+ *
+ * Return value: 0 on success, a positive cudaError_t from the launch, or a
+ * negative EXK_E* argument error (exk_error_string() describes every code).
+ * Faults found by the kernels themselves (a spin-wait that ran out of time, a
+ * raw-pool index past the pool) are written as a nonzero EXK_S* code to the
+ * caller's device status word, which the caller reads when it next syncs.
+ *
+ * Compressed format (per 16-token page, per KV head, per channel; D = 128):
+ *   sm      uint8 [B, TS, H, 128]     sign bit | 7 mantissa bits, unchanged
+ *   code    uint8 [B, TS, H, 64]      4-bit exponent offsets; byte j holds
+ *                                     channel j (low nibble) and j+64 (high)
+ *   base    uint8 [B, TS/16, H, 128]  bit 7: the group holds zeros (code 0 =
+ *                                     exponent 0); bits 0-6: exponent base
+ *   rowmask int32 [B, TS/16, H]       bit p: token p of the page is raw
+ *   rowoff  int32 [B, TS/16, H]       pool index of the page's first raw row
+ *   raw     bf16  [rows, 128]         raw rows; a page's raw rows are adjacent
+ * (reference: exactkv/codec.py:10-19, allocation exactkv/cache.py:24-32).
+ */
+#ifndef EXACTKV_B200_H
+#define EXACTKV_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define EXK_HEAD_DIM 128
+#define EXK_PAGE 16
+
+/* argument errors (negative return values) */
+#define EXK_EARG      (-1)  /* shape or count out of range */
+#define EXK_EALIGN    (-2)  /* a pointer or stride breaks the 16-byte rule */
+#define EXK_ETMAP     (-3)  /* cuTensorMapEncodeTiled rejected a tensor map */
+#define EXK_EDRIVER   (-4)  /* the driver entry point could not be resolved */
+#define EXK_EHEADS    (-5)  /* more than 16 query heads per KV head */
+
+/* device status codes (written to the caller's int32 status word) */
+#define EXK_S_OK             0
+#define EXK_S_FULL_TIMEOUT   1  /* a consumer waited > 2 s for a staged page */
+#define EXK_S_EMPTY_TIMEOUT  2  /* the TMA producer waited > 2 s for a free slot */
+#define EXK_S_RAW_INDEX      3  /* rowoff/rowmask pointed past the raw pool */
+#define EXK_S_CHAIN_TIMEOUT  4  /* encoder CTA waited > 2 s for its predecessor */
+#define EXK_S_DRAIN_TIMEOUT  5  /* in-flight TMA copies did not land within 2 s */
+
+/* One compressed cache (keys or values of one layer): the six buffers of the
+ * format above. raw_rows is the number of rows `raw` holds; indices at or
+ * past it are reported (EXK_S_RAW_INDEX) and read as zero, never loaded. */
+typedef struct exk_cview {
+  const uint8_t *sm;
+  const uint8_t *code;
+  const uint8_t *base;
+  const int32_t *rowmask;
+  const int32_t *rowoff;
+  const uint16_t *raw;
+  int64_t raw_rows;
+} exk_cview;
+
+/* Split-K partials, laid out as the reference's workspace
+ * (exactkv/kernels.py:290): o fp32 [rows, ns, 128] (unnormalised),
+ * m fp32 [rows, ns] (running max of base-2 scores), l fp32 [rows, ns]
+ * (sum of exp2(s - m)); rows = B * Hq. */
+typedef struct exk_partials {
+  float *o;
+  float *m;
+  float *l;
+  int32_t ns;
+  int32_t split_len;
+} exk_partials;
+
+/* Split plan: number of token splits per (sequence, KV head) and their length
+ * (a multiple of 16), chosen so that B*Hkv*ns work items spread evenly over
+ * `num_ctas` persistent CTAs (one per SM). Replaces choose_split()
+ * (exactkv/kernels.py:273-277); the layout depends only on the arguments, so
+ * the compressed and bf16 kernels and every GPU of a KV split share it. */
+int exk_plan_splits(int B, int Hkv, int T, int num_ctas, int32_t *ns, int32_t *split_len);
+
+/* Number of SMs of a device (the default `num_ctas`). */
+int exk_num_sms(int device);
+
+/* Split-K decode attention over the compressed cache, splits [s0, s1) of the
+ * plan in `ws`. q: bf16 [B, Hq, 128] contiguous, Hq = G * Hkv, 1 <= G <= 16.
+ * consumer_warps: 4 or 8. Replaces _split_c_kernel (exactkv/kernels.py:142-165). */
+int exk_attn_split_compressed(const uint16_t *q, const exk_cview *k, const exk_cview *v,
+                              int B, int TS, int Hkv, int Hq, int T, int s0, int s1,
+                              const exk_partials *ws, int consumer_warps, float qk_scale,
+                              int32_t *status, int device, void *stream);
+
+/* The same computation on uncompressed bf16 K, V [B, TS, Hkv, 128]
+ * (contiguous). Bit-identical to exk_attn_split_compressed on the same values,
+ * plan and consumer_warps. Replaces _split_ref_kernel (exactkv/kernels.py:168-194). */
+int exk_attn_split_bf16(const uint16_t *q, const uint16_t *k, const uint16_t *v,
+                        int B, int TS, int Hkv, int Hq, int T, int s0, int s1,
+                        const exk_partials *ws, int consumer_warps, float qk_scale,
+                        int32_t *status, int device, void *stream);
+
+/* Merge of the split partials into bf16 out [rows, 128]:
+ * out = sum_s o_s 2^(m_s - M) / sum_s l_s 2^(m_s - M), M = max_s m_s.
+ * Replaces _reduce_kernel (exactkv/kernels.py:33-43). */
+int exk_attn_merge(const exk_partials *ws, int rows, uint16_t *out, int device, void *stream);
+
+/* Page encoder: encodes nb sequences x npg pages of `src` (bf16 bits, element
+ * strides s_b, s_pg, s_p, s_h for sequence, page, token, head; channels
+ * contiguous) into sequences b0.. and pages pg0.. of the buffers. Raw rows get
+ * pool slots cnt, cnt+1, ... in (sequence, page, head) order — the order of
+ * the reference's encode_reference — through a chained scan over CTAs;
+ * `cnt` advances even past raw_cap, but slots at or past raw_cap are not
+ * written (the caller grows the pool and encodes again). `chain` is 2 int32
+ * of zero-initialised scratch, private to the stream; the kernel leaves it
+ * zero. Replaces _encode_pages_kernel/encode_pages (exactkv/kernels.py:233-268, 340-346). */
+int exk_encode_pages(const uint16_t *src, int64_t s_b, int64_t s_pg, int64_t s_p, int64_t s_h,
+                     uint8_t *sm, uint8_t *code, uint8_t *base, int32_t *rowmask, int32_t *rowoff,
+                     uint16_t *raw, int64_t raw_cap, int32_t *cnt, int32_t *chain,
+                     int b0, int pg0, int nb, int npg, int H, int TS,
+                     int32_t *status, int device, void *stream);
+
+/* Compressed cache -> bf16 out [B, T, H, 128] through the attention kernel's
+ * decoder. Replaces _dec_only_kernel/decode_to_bf16 (exactkv/kernels.py:197-211, 331-337). */
+int exk_decode_to_bf16(const exk_cview *c, int B, int TS, int H, int T, uint16_t *out,
+                       int32_t *status, int device, void *stream);
+
+/* Human-readable text for a return value or a device status code. */
+const char *exk_error_string(int code);
+const char *exk_status_string(int code);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EXACTKV_B200_H */

@@ -1,0 +1,142 @@
+"""Decode attention on the B200 kernels.
+
+  * compressed == bf16 sibling, bit for bit (reference tests/test_exactkv.py:61-78,
+    same shapes and data recipe, both consumer-warp counts);
+  * both within oracle.attention.tolerance of the CPU restatement of the
+    reference's split-K attention and of the float64 attention;
+  * config 1 (golden float64 attention from the reference's test formula).
+"""
+import numpy as np
+import pytest
+import torch
+
+import exactkv_b200 as ekv
+from exactkv_b200 import kernels, synthetic
+from gpu_util import same_bits, to_bits, to_dev
+from oracle import attention as oatt
+from oracle.bf16 import bits_to_f32
+from synth_np import CONFIG1, config1_inputs
+
+pytestmark = pytest.mark.gpu
+
+REF_SHAPES = [(1, 4096, 28, 4), (3, 1000, 32, 8), (2, 333, 32, 32), (4, 17, 16, 2)]
+
+
+def _compress(x):
+    """[B, TS, H, D] bf16 -> a CompressedKV holding all TS tokens (prefill path)."""
+    B, TS, H, D = x.shape
+    c = ekv.CompressedKV(B, TS, H, D, reserve=1.0)
+    for b in range(B):
+        c.prefill_slot(b, x[b:b + 1].contiguous())
+    return c
+
+
+def _ref_test_data(B, T, Hq, Hkv, seed):
+    """The reference test's recipe (tests/test_exactkv.py:64-69) on a CPU generator."""
+    g = torch.Generator().manual_seed(seed)
+    TS = -(-T // 16) * 16
+    scale = torch.exp(torch.randn(Hkv, 128, generator=g) * 0.7)
+    k = (torch.randn(B, TS, Hkv, 128, generator=g) * scale).to(torch.bfloat16)
+    v = torch.randn(B, TS, Hkv, 128, generator=g).to(torch.bfloat16)
+    k[:, ::97, :, 3] = 0.0
+    q = (torch.randn(B, Hq, 128, generator=g) * 0.3).to(torch.bfloat16)
+    return q.cuda(), k.cuda(), v.cuda()
+
+
+def _check_close(o, q, k, v, T, ref=None):
+    qb, kb, vb = to_bits(q), to_bits(k), to_bits(v)
+    ref = oatt.attention_f64(qb, kb, vb, T) if ref is None else ref
+    tol = oatt.tolerance(qb, kb, vb, T, ref)
+    got = bits_to_f32(to_bits(o)).astype(np.float64)
+    ratio = np.abs(got - ref) / tol
+    assert ratio.max() <= 1.0, f"max err/tol {ratio.max():.3f}"
+    orc = bits_to_f32(oatt.attention(qb, kb, vb, T)).astype(np.float64)
+    ratio_o = np.abs(got - orc) / oatt.tolerance(qb, kb, vb, T, orc)
+    assert ratio_o.max() <= 1.0, f"vs oracle: max err/tol {ratio_o.max():.3f}"
+    return ratio.max()
+
+
+@pytest.mark.parametrize("B,T,Hq,Hkv", REF_SHAPES)
+def test_attention_bit_identical_and_close(B, T, Hq, Hkv):
+    q, k, v = _ref_test_data(B, T, Hq, Hkv, seed=1 + B + T)
+    kc, vc = _compress(k), _compress(v)
+    for nw in (4, 8):
+        o_c = kernels.attention_compressed(q, kc.buffers(), vc.buffers(), T, num_warps=nw)
+        o_r = kernels.attention_reference(q, k, v, T, num_warps=nw)
+        assert same_bits(o_c, o_r), (B, T, Hq, Hkv, nw)
+        o_obj = kernels.attention_compressed(q, kc, vc, T, num_warps=nw)
+        assert same_bits(o_obj, o_c)
+        _check_close(o_c, q, k, v, T)
+    kernels.check_status()
+
+
+@pytest.mark.parametrize("case", CONFIG1, ids=[c["name"] for c in CONFIG1])
+def test_attention_config1(golden, case):
+    qn, kn, vn = config1_inputs(case)
+    T = case["T"]
+    q, k, v = to_dev(qn), to_dev(kn), to_dev(vn)
+    # prefill exactly T tokens: full pages encoded, the tail page raw in the pool
+    B, TS, H, D = k.shape
+    kc, vc = ekv.CompressedKV(B, TS, H, D), ekv.CompressedKV(B, TS, H, D)
+    for b in range(B):
+        kc.prefill_slot(b, k[b:b + 1, :T].contiguous())
+        vc.prefill_slot(b, v[b:b + 1, :T].contiguous())
+    o_c = ekv.decode_attention(q, kc, vc)
+    o_r = kernels.attention_reference(q, k, v, T)
+    assert same_bits(o_c, o_r)
+    _check_close(o_c, q, k, v, T, ref=golden["config1"][f"{case['name']}/attn_f64"])
+    kernels.check_status()
+
+
+@pytest.mark.parametrize("B,T,Hq,Hkv", [(1, 700, 12, 1), (2, 300, 16, 1), (2, 257, 9, 1), (1, 64, 1, 1)])
+def test_attention_head_groups(B, T, Hq, Hkv):
+    """G > 8 uses two n-tiles of heads; G = 1 pads seven."""
+    q, k, v = _ref_test_data(B, T, Hq, Hkv, seed=7)
+    kc, vc = _compress(k), _compress(v)
+    o_c = kernels.attention_compressed(q, kc, vc, T)
+    o_r = kernels.attention_reference(q, k, v, T)
+    assert same_bits(o_c, o_r)
+    _check_close(o_c, q, k, v, T)
+    kernels.check_status()
+
+
+def test_attention_llama_shaped_synthetic():
+    """Llama-3.1-8B head layout (32 q / 8 kv) on the benchmark distribution
+    (RoPE theta 5e5, 0.04% zeros, 0.3% forced raw rows), several splits per sequence."""
+    B, T, Hq, Hkv = 4, 4096, 32, 8
+    k = synthetic.make_kv(B, T, Hkv, seed=11, theta=5e5, key=True)
+    v = synthetic.make_kv(B, T, Hkv, seed=12, theta=5e5, key=False)
+    q = synthetic.make_q(B, Hq, seed=13)
+    kc, vc = _compress(k), _compress(v)
+    assert int(kc.cnt.item()) > 0 and int(vc.cnt.item()) > 0
+    ns, _ = kernels.plan_splits(B, Hkv, T)
+    assert ns > 1
+    o_c = ekv.decode_attention(q, kc, vc)
+    o_r = kernels.attention_reference(q, k, v, T)
+    assert same_bits(o_c, o_r)
+    _check_close(o_c, q, k, v, T)
+    kernels.check_status()
+
+
+def test_attention_split_subsets_match_full_run():
+    """Running the plan's splits in two launches ([0, s) and [s, ns)) writes the same
+    partials as one launch — the per-GPU step of a KV-sequence split."""
+    B, T, Hq, Hkv = 1, 8192, 32, 8
+    k = synthetic.make_kv(B, T, Hkv, seed=21, key=True)
+    v = synthetic.make_kv(B, T, Hkv, seed=22, key=False)
+    q = synthetic.make_q(B, Hq, seed=23)
+    kc, vc = _compress(k), _compress(v)
+    ns, sl = kernels.plan_splits(B, Hkv, T)
+    assert ns >= 2
+    ws_a = kernels._workspace(q.device, 1, B * Hq, ns, sl)   # private keys: not shared with other calls
+    ws_b = kernels._workspace(q.device, 2, B * Hq, ns, sl)
+    kernels.attention_split(q, kc, vc, T, ws_a, 0, ns)
+    s = ns // 2
+    kernels.attention_split(q, kc, vc, T, ws_b, 0, s)
+    kernels.attention_split(q, kc, vc, T, ws_b, s, ns)
+    for x, y in zip(ws_a[:3], ws_b[:3]):
+        assert torch.equal(x, y)
+    out = torch.empty_like(q)
+    kernels.merge_partials(ws_b, B * Hq, out)
+    assert same_bits(out, ekv.decode_attention(q, kc, vc))
+    kernels.check_status()
