@@ -62,6 +62,12 @@ struct alignas(64) AttnMaps {
 
 template <bool COMP, int NT, int NWC>
 struct Smem {
+  // Phase safety of the ring: a consumer waits on round r of a slot only after
+  // round r-1 was consumed. Within an item, page p and page p-kRing belong to
+  // the same warp (kRing is a multiple of NWC) and are handled in order; pages
+  // of earlier items were all consumed before the item-end barrier. So a
+  // parity wait never sees a phase two rounds old.
+  static_assert(kRing % NWC == 0, "ring size must be a multiple of the consumer warps");
   static constexpr int kSlotBytes = COMP ? 6400 : 8192;
   static constexpr int kHeads = 8 * NT;
   static constexpr int kRingBytes = kRing * kSlotBytes;

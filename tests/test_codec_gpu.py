@@ -124,14 +124,16 @@ def test_gpu_encoder_pool_overflow_counts_and_skips():
     ref = ocodec.encode(x)
     nraw = ref["raw"].shape[0]
     assert nraw > 8
-    c = ekv.CompressedKV(1, 64, 4, 128, reserve=0.0)
-    c.cap = 8                                             # pool smaller than needed
-    c._rebind()
+    c = ekv.CompressedKV(1, 64, 4, 128)
+    buf = c._buf()
+    buf["cap"] = 8                                        # a pool smaller than needed
     sentinel = torch.full_like(c.raw, 7.0)
     c.raw.copy_(sentinel)
     xs = to_dev(x)
-    kernels.encode_pages(xs, (xs.stride(0), 16 * xs.stride(1), xs.stride(1), xs.stride(2)), c._buf(), 0, 0, 1, 4)
+    kernels.encode_pages(xs, (xs.stride(0), 16 * xs.stride(1), xs.stride(1), xs.stride(2)), buf, 0, 0, 1, 4)
     assert int(c.cnt.item()) == nraw
     assert np.array_equal(to_bits(c.raw[:8]), ref["raw"][:8])
     assert same_bits(c.raw[8:], sentinel[8:])
+    for f in ("sm", "code", "base", "rowmask", "rowoff"):
+        assert np.array_equal(getattr(c, f).cpu().numpy(), ref[f]), f
     kernels.check_status()
