@@ -65,6 +65,8 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--num-warps", type=int, default=8)
+    ap.add_argument("--quick", action="store_true",
+                    help="few launches for profiling: no warm loop, L2-flushed pass, e2e or CPU baseline")
     return ap.parse_args()
 
 
@@ -256,7 +258,7 @@ def run_ours(a, rank, world, local):
     with clocks:
         for _ in range(a.warmup):
             step()
-        warm_until = time.perf_counter() + 0.3     # keep the GPU busy long enough for clock samples
+        warm_until = time.perf_counter() + (0.0 if a.quick else 0.3)   # long enough for clock samples
         while time.perf_counter() < warm_until:
             step()
         total_ms, launch_ms = timed(step, a.steps, per_launch=True)
@@ -268,8 +270,10 @@ def run_ours(a, rank, world, local):
     ms_per_step = total_ms / a.steps
     split_us = statistics.mean(launch_ms) * 1e3
 
-    _, flushed = timed(step, min(a.steps, 50), per_launch=True, flush_between=True)
-    split_us_flushed = statistics.median(flushed) * 1e3
+    split_us_flushed = None
+    if not a.quick:
+        _, flushed = timed(step, min(a.steps, 50), per_launch=True, flush_between=True)
+        split_us_flushed = round(statistics.median(flushed) * 1e3, 2)
     for _ in range(3):
         sibling_step()
     sib_ms, _ = timed(sibling_step, a.steps)
@@ -281,11 +285,11 @@ def run_ours(a, rank, world, local):
     traffic = profiled_traffic()
 
     e2e = None
-    if not a.no_e2e:
+    if not (a.no_e2e or a.quick):
         e2e = run_e2e(a, kc, vc, B, Hq, Hkv, T, dev, world, raw_rows, ns)
 
     cpu = None
-    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+    if rank == 0 and world == 1 and not (a.no_cpu_baseline or a.quick):
         cpu = cpu_sample(T, Hkv, Hq)
     rec = {
         "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world, "steps": a.steps,
@@ -296,7 +300,7 @@ def run_ours(a, rank, world, local):
                        consumer_warps=a.num_warps),
         "attn_us_per_call": round(ms_per_step * 1e3, 2),
         "split_kernel_us": round(split_us, 2),
-        "split_kernel_us_l2_flushed": round(split_us_flushed, 2),
+        "split_kernel_us_l2_flushed": split_us_flushed,
         "compressed_bytes_per_call": nbytes, "raw_rows": raw_rows,
         "raw_row_fraction": round(raw_rows / (2 * B * T * Hkv), 5),
         "bits_per_value": round(8 * nbytes / (2 * B * T * Hkv * 128), 3),

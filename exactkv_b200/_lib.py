@@ -40,6 +40,8 @@ _SIGNATURES.update({
                                  c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int, c_int, c_int,
                                  c_int, c_int, c_int, c_void_p, c_int, c_void_p]),
     "exk_decode_to_bf16": (c_int, [_P(CView), c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_void_p]),
+    "exk_attention_compressed_noalloc": (c_int, [c_void_p, _P(CView), _P(CView), c_int, c_int, c_int, c_int, c_int,
+                                                 c_int, c_float, c_void_p, c_void_p, c_int, c_void_p]),
     "exk_error_string": (ctypes.c_char_p, [c_int]),
     "exk_status_string": (ctypes.c_char_p, [c_int]),
 })
@@ -47,7 +49,7 @@ _SIGNATURES.update({
 
 def _load():
     if not os.path.exists(LIB_PATH):
-        raise ImportError(f"exactkv_b200: {LIB_PATH} is not built; run `python -m exactkv_b200.build` "
+        raise ImportError(f"exactkv_b200: {LIB_PATH} is not built; run `python exactkv_b200/build.py` "
                           "(there is no CPU or Triton fallback)")
     lib = ctypes.CDLL(LIB_PATH)
     for name, (res, args) in _SIGNATURES.items():

@@ -1,8 +1,11 @@
 """Builds libexactkv_b200.so (sm_100a) in-tree with nvcc.
 
-    python -m exactkv_b200.build            # compile if a source is newer than the library
-    python -m exactkv_b200.build --force    # always recompile
-    python -m exactkv_b200.build --ptxas-v  # also print ptxas register/spill/smem report
+    python exactkv_b200/build.py            # compile if a source is newer than the library
+    python exactkv_b200/build.py --force    # always recompile
+    python exactkv_b200/build.py --ptxas-v  # also print ptxas register/spill/smem report
+
+Run it as a script (or through __graft_entry__.build()): importing the
+exactkv_b200 package loads the library, so the package cannot build itself.
 """
 import argparse
 import os
@@ -13,7 +16,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libexactkv_b200.so")
-SOURCES = ["exk_host.cu", "exk_attention.cu", "exk_codec.cu"]
+SOURCES = ["exk_host.cu", "exk_attention.cu", "exk_codec.cu", "exk_noalloc.cu"]
 HEADERS = ["exk_device.cuh", "exk_host.h", os.path.join("..", "..", "include", "exactkv_b200.h")]
 
 NVCC_FLAGS = [

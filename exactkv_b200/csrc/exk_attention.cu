@@ -1,15 +1,17 @@
 // Split-K decode attention over the exponent-coded bf16 KV cache (sm_100a),
 // its uncompressed bf16 sibling, and the split merge.
 //
-// Work decomposition. A work item is one (sequence b, KV head hk, token split)
-// of the plan; persistent CTAs (one per SM) take items round-robin. Inside a
-// CTA one producer warp streams the item's 16-token pages through a 16-slot
-// shared-memory ring with TMA (cp.async.bulk.tensor, 128B/64B swizzle, no
-// multicast) and mbarriers; consumer warp w takes pages w, w+NWC, ... of the
-// item. Each consumer rebuilds K and V in registers straight into bf16 mma
-// fragments, runs the online softmax on its own pages, and at the end of the
-// item the warps' (m, l, acc) are merged through shared memory in fixed warp
-// order and written as the item's split partial.
+// Work decomposition. A work item is one (sequence b, group of HG KV heads,
+// token split) of the plan; persistent CTAs (one per SM) take items
+// round-robin. The HG heads of a page range are one contiguous region of each
+// cache buffer ([B, TS, H, *] layout), so one producer warp streams a stage =
+// WPH consecutive 16-token pages of all HG heads with one TMA box per field
+// (cp.async.bulk.tensor, 128B/64B swizzle, no multicast) into a ring of
+// mbarrier-guarded stages. The NWC = HG x WPH consumer warps are (head, page
+// phase) pairs: every warp consumes every stage, rebuilding its head's K and V
+// of its page in registers straight into bf16 mma fragments and running the
+// online softmax; with WPH > 1 the page phases of a head are merged through
+// shared memory at the end of the item, in fixed order.
 //
 // Tensor-core mapping ("swapped" GQA): per 16-token page the warp computes
 //   S^T[16 tok x 8 heads]  = K[16 x 128] . Q^T[128 x 8]     (8 mma, k = channels)
@@ -22,6 +24,7 @@
 // and differ only in how a lane fills its fragment registers; the registers
 // hold the same bf16 bits in the same slots, so every mma, softmax step and
 // merge runs identically (the property exactkv/kernels.py:10-18 relies on).
+#include <algorithm>
 #include <cfloat>
 #include <cuda.h>
 
@@ -30,8 +33,7 @@
 
 namespace exk {
 
-constexpr int kRing = 16;            // pages in flight per CTA
-constexpr int kAccPitch = 132;       // floats per head row of the merge buffer (bank padding)
+constexpr int kAccPitch = 132;            // floats per head row of the merge buffer (bank padding)
 constexpr uint32_t kSigma = 0x27146350u;  // mma row r (0..7) -> page token sigma(r), nibble r
 
 // Token of the page that mma row r (0..15) holds. The permutation spreads the
@@ -51,7 +53,7 @@ struct AttnArgs {
   float* ws_l;
   int32_t* status;
   int B, TS, NP, Hkv, Hq, G, T;
-  int ns, split_len, s0, nsl, n_items;
+  int ns, split_len, s0, nsl, n_items, ngroups;
   float qk_scale;
 };
 
@@ -60,58 +62,74 @@ struct alignas(64) AttnMaps {
   CUtensorMap m[6];
 };
 
-template <bool COMP, int NT, int NWC>
-struct Smem {
-  // Phase safety of the ring: a consumer waits on round r of a slot only after
-  // round r-1 was consumed. Within an item, page p and page p-kRing belong to
-  // the same warp (kRing is a multiple of NWC) and are handled in order; pages
-  // of earlier items were all consumed before the item-end barrier. So a
-  // parity wait never sees a phase two rounds old.
-  static_assert(kRing % NWC == 0, "ring size must be a multiple of the consumer warps");
-  static constexpr int kSlotBytes = COMP ? 6400 : 8192;
-  static constexpr int kHeads = 8 * NT;
-  static constexpr int kRingBytes = kRing * kSlotBytes;
-  static constexpr int kAccBytes = NWC * kHeads * kAccPitch * 4;
+// Heads per CTA for a KV head count: the largest power of two <= 8 dividing it.
+__host__ __device__ constexpr int head_group(int hkv) {
+  return hkv % 8 == 0 ? 8 : hkv % 4 == 0 ? 4 : hkv % 2 == 0 ? 2 : 1;
+}
+
+template <bool COMP, int NT, int NWC, int HG>
+struct Cfg {
+  static_assert(NWC % HG == 0, "heads per CTA must divide the consumer warps");
+  static constexpr int kWph = NWC / HG;                       // page phases per head
+  static constexpr int kTile = COMP ? 6400 : 8192;           // one head x one page, K and V
+  static constexpr int kStageBytes = NWC * kTile;
+  static constexpr int kHeads = 8 * NT;                      // query heads per warp (padded)
+  static constexpr int kMergeBytes = kWph > 1 ? HG * kHeads * kAccPitch * 4 : 0;
   static constexpr int kMLBytes = 2 * NWC * kHeads * 4;
-  static constexpr int kBarBytes = 2 * kRing * 8 + 16;
-  static constexpr int kBytes = kRingBytes + kAccBytes + kMLBytes + kBarBytes + 1024;  // + alignment slack
-  static constexpr uint32_t kTxBytes = COMP ? 2u * (2048u + 1024u + 128u) : 4u * 2048u;
+  static constexpr int kBudget = 224 * 1024 - kMergeBytes - kMLBytes - 1024;
+  static constexpr int kStages = (kBudget / kStageBytes) > 4 ? 4 : (kBudget / kStageBytes);
+  static_assert(kStages >= 2, "shared memory too small for two stages");
+  static constexpr int kRingBytes = kStages * kStageBytes;
+  static constexpr int kBarBytes = 2 * kStages * 8 + 16;
+  static constexpr int kBytes = kRingBytes + kMergeBytes + kMLBytes + kBarBytes + 1024;  // + alignment slack
+  static constexpr uint32_t kTxBytes = static_cast<uint32_t>(kStageBytes);
 };
 
-// Shared-memory addresses of one ring slot. Compressed layout: sm tiles
-// [ring][K,V][16 rows x 128 B] (128B swizzle), code tiles [ring][K,V][16 x 64 B]
-// (64B swizzle), base rows [ring][K,V][128 B]. bf16 layout:
-// [ring][K lo, K hi, V lo, V hi][16 rows x 128 B] (128B swizzle), lo = channels 0-63.
+// Shared-memory layout of one stage. Compressed: sm [K,V][HG][16*WPH rows][128 B]
+// (128B swizzle), code [K,V][HG][16*WPH][64 B] (64B swizzle), base [K,V][HG][WPH][128 B].
+// bf16: [K lo, K hi, V lo, V hi][HG][16*WPH][128 B] (128B swizzle; lo = channels 0-63).
+// The tile of (head h, page phase ph) starts at a 1024-byte multiple, so the
+// swizzle phase of its row r is r & 7 whatever h and ph are.
 struct Slot {
-  uint8_t* p[6];
+  const uint8_t* p[6];
 };
 
-template <bool COMP>
-__device__ __forceinline__ Slot slot_ptrs(uint8_t* ring, int s) {
+template <bool COMP, int NWC, int HG>
+__device__ __forceinline__ Slot tile_ptrs(const uint8_t* stage, int h, int ph) {
+  constexpr int WPH = NWC / HG;
+  const int u = h * WPH + ph;  // tile index within a field
   Slot o;
   if constexpr (COMP) {
-    uint8_t* sm = ring + s * 4096;
-    uint8_t* cd = ring + kRing * 4096 + s * 2048;
-    uint8_t* bs = ring + kRing * 6144 + s * 256;
-    o.p[0] = sm; o.p[1] = cd; o.p[2] = bs;
-    o.p[3] = sm + 2048; o.p[4] = cd + 1024; o.p[5] = bs + 128;
+    const uint8_t* sm = stage;
+    const uint8_t* cd = stage + NWC * 4096;
+    const uint8_t* bs = stage + NWC * 6144;
+    o.p[0] = sm + u * 2048;
+    o.p[1] = cd + u * 1024;
+    o.p[2] = bs + u * 128;
+    o.p[3] = sm + NWC * 2048 + u * 2048;
+    o.p[4] = cd + NWC * 1024 + u * 1024;
+    o.p[5] = bs + NWC * 128 + u * 128;
   } else {
-    uint8_t* b = ring + s * 8192;
-    o.p[0] = b; o.p[1] = b + 2048; o.p[2] = b + 4096; o.p[3] = b + 6144; o.p[4] = nullptr; o.p[5] = nullptr;
+    o.p[0] = stage + u * 2048;
+    o.p[1] = stage + NWC * 2048 + u * 2048;
+    o.p[2] = stage + 2 * NWC * 2048 + u * 2048;
+    o.p[3] = stage + 3 * NWC * 2048 + u * 2048;
+    o.p[4] = nullptr;
+    o.p[5] = nullptr;
   }
   return o;
 }
 
 struct Item {
-  int b, hk, split, tok0, tok1, page0, npages;
+  int b, hg, split, tok0, tok1, page0, npages;
 };
 
 __device__ __forceinline__ Item decode_item(const AttnArgs& a, int item) {
   Item it;
-  const int bh = item / a.nsl;
+  const int bg = item / a.nsl;
   it.split = a.s0 + item % a.nsl;
-  it.b = bh / a.Hkv;
-  it.hk = bh % a.Hkv;
+  it.b = bg / a.ngroups;
+  it.hg = bg % a.ngroups;
   it.tok0 = it.split * a.split_len;
   it.tok1 = min(it.tok0 + a.split_len, a.T);
   it.page0 = it.tok0 / kP;
@@ -328,14 +346,21 @@ __device__ __forceinline__ void attend_page(const Slot& s, const PageMeta& pm, i
     const uint32_t fl = (COMP ? pm.rm[0] : 0u) | tailmask;
     if (fl != 0u) fix_k_rows(fl, pm.rm[0], pm.ro[0], COMP ? a.raw[0] : nullptr, a.raw_rows[0], a.status, vr, g, t, kw);
   }
+  // two independent accumulation chains (low and high channel halves), summed
   float sc[NT][4];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
+    float s1[4] = {0.f, 0.f, 0.f, 0.f};
     sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
 #pragma unroll
-    for (int kk = 0; kk < 8; ++kk)
+    for (int kk = 0; kk < 4; ++kk) {
       mma_bf16(sc[nt], kw[0][2 * kk], kw[1][2 * kk], kw[0][2 * kk + 1], kw[1][2 * kk + 1], qf[nt][2 * kk],
                qf[nt][2 * kk + 1]);
+      mma_bf16(s1, kw[0][2 * kk + 8], kw[1][2 * kk + 8], kw[0][2 * kk + 9], kw[1][2 * kk + 9], qf[nt][2 * kk + 8],
+               qf[nt][2 * kk + 9]);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) sc[nt][i] += s1[i];
   }
 
   // ---- V fragments (issued before the softmax so the shared loads overlap it)
@@ -390,14 +415,14 @@ __device__ __forceinline__ void attend_page(const Slot& s, const PageMeta& pm, i
   }
 }
 
+
 template <int NT>
-__device__ __forceinline__ void load_q(const AttnArgs& a, const Item& it, int g, int t, uint32_t (&qf)[NT][16]) {
+__device__ __forceinline__ void load_q(const AttnArgs& a, int b, int hk, int g, int t, uint32_t (&qf)[NT][16]) {
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
     const int h = nt * 8 + g;
     if (h < a.G) {
-      const uint4* qr =
-          reinterpret_cast<const uint4*>(a.q + (static_cast<int64_t>(it.b) * a.Hq + it.hk * a.G + h) * kD);
+      const uint4* qr = reinterpret_cast<const uint4*>(a.q + (static_cast<int64_t>(b) * a.Hq + hk * a.G + h) * kD);
       const uint4 x0 = qr[2 * t], x1 = qr[2 * t + 1], x2 = qr[8 + 2 * t], x3 = qr[8 + 2 * t + 1];
       const uint32_t w[16] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w,
                               x2.x, x2.y, x2.z, x2.w, x3.x, x3.y, x3.z, x3.w};
@@ -411,10 +436,10 @@ __device__ __forceinline__ void load_q(const AttnArgs& a, const Item& it, int g,
 }
 
 template <bool COMP>
-__device__ __forceinline__ PageMeta load_meta(const AttnArgs& a, const Item& it, int pg) {
+__device__ __forceinline__ PageMeta load_meta(const AttnArgs& a, int b, int hk, int pg) {
   PageMeta pm;
   if constexpr (COMP) {
-    const int64_t idx = (static_cast<int64_t>(it.b) * a.NP + pg) * a.Hkv + it.hk;
+    const int64_t idx = (static_cast<int64_t>(b) * a.NP + pg) * a.Hkv + hk;
     pm.rm[0] = static_cast<uint32_t>(__ldg(a.rowmask[0] + idx)) & 0xFFFFu;
     pm.rm[1] = static_cast<uint32_t>(__ldg(a.rowmask[1] + idx)) & 0xFFFFu;
     pm.ro[0] = __ldg(a.rowoff[0] + idx);
@@ -428,25 +453,30 @@ __device__ __forceinline__ PageMeta load_meta(const AttnArgs& a, const Item& it,
 
 // ------------------------------------------------------------------ kernel
 
-template <bool COMP, int NT, int NWC>
+template <bool COMP, int NT, int NWC, int HG>
 __global__ void __launch_bounds__((NWC + 1) * 32, 1)
     attn_split_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ AttnMaps tm) {
-  using L = Smem<COMP, NT, NWC>;
-  constexpr int H8 = L::kHeads;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float* macc = reinterpret_cast<float*>(ring + L::kRingBytes);
-  float* mbuf = macc + NWC * H8 * kAccPitch;
+  using C = Cfg<COMP, NT, NWC, HG>;
+  constexpr int S = C::kStages;
+  constexpr int WPH = C::kWph;
+  constexpr int H8 = C::kHeads;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // Align by offsetting the __shared__ array itself (not through an integer
+  // round trip), so every access below stays a shared-memory access (LDS/STS)
+  // rather than a generic one.
+  uint8_t* ring = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+  float* macc = reinterpret_cast<float*>(ring + C::kRingBytes);
+  float* mbuf = reinterpret_cast<float*>(ring + C::kRingBytes + C::kMergeBytes);
   float* lbuf = mbuf + NWC * H8;
   uint64_t* full = reinterpret_cast<uint64_t*>(lbuf + NWC * H8);
-  uint64_t* empty = full + kRing;
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kRing);
+  uint64_t* empty = full + S;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + S);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kRing; ++i) {
+    for (int i = 0; i < S; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], 1);
+      mbar_init(&empty[i], NWC);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -458,13 +488,14 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
     if (lane != 0) return;
     constexpr int nmaps = COMP ? 6 : 2;
     for (int i = 0; i < nmaps; ++i) prefetch_tmap(&tm.m[i]);
-    uint32_t gi = 0;
+    uint32_t gs = 0;  // stages issued
     bool ok = true;
     for (int item = blockIdx.x; ok && item < a.n_items; item += gridDim.x) {
       const Item it = decode_item(a, item);
-      for (int p = 0; p < it.npages; ++p, ++gi) {
-        const int slot = gi % kRing;
-        const uint32_t round = gi / kRing;
+      const int nst = (it.npages + WPH - 1) / WPH;
+      for (int s = 0; s < nst; ++s, ++gs) {
+        const int slot = gs % S;
+        const uint32_t round = gs / S;
         if (round > 0 && !mbar_wait(&empty[slot], (round - 1) & 1u)) {
           set_status(a.status, EXK_S_EMPTY_TIMEOUT);
           *abort_flag = 1;
@@ -475,29 +506,30 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
           ok = false;
           break;
         }
-        const int pg = it.page0 + p;
+        const int pg = it.page0 + s * WPH;
         const int row = it.b * a.TS + pg * kP;
-        const Slot s = slot_ptrs<COMP>(ring, slot);
-        mbar_arrive_expect_tx(&full[slot], L::kTxBytes);
+        const int h0 = it.hg * HG;
+        uint8_t* st = ring + slot * C::kStageBytes;
+        mbar_arrive_expect_tx(&full[slot], C::kTxBytes);
         if constexpr (COMP) {
           const int prow = it.b * a.NP + pg;
-          tma_load_3d(s.p[0], &tm.m[0], 0, it.hk, row, &full[slot]);
-          tma_load_3d(s.p[1], &tm.m[1], 0, it.hk, row, &full[slot]);
-          tma_load_3d(s.p[2], &tm.m[2], 0, it.hk, prow, &full[slot]);
-          tma_load_3d(s.p[3], &tm.m[3], 0, it.hk, row, &full[slot]);
-          tma_load_3d(s.p[4], &tm.m[4], 0, it.hk, row, &full[slot]);
-          tma_load_3d(s.p[5], &tm.m[5], 0, it.hk, prow, &full[slot]);
+          tma_load_3d(st, &tm.m[0], 0, row, h0, &full[slot]);
+          tma_load_3d(st + NWC * 2048, &tm.m[3], 0, row, h0, &full[slot]);
+          tma_load_3d(st + NWC * 4096, &tm.m[1], 0, row, h0, &full[slot]);
+          tma_load_3d(st + NWC * 5120, &tm.m[4], 0, row, h0, &full[slot]);
+          tma_load_3d(st + NWC * 6144, &tm.m[2], 0, prow, h0, &full[slot]);
+          tma_load_3d(st + NWC * 6272, &tm.m[5], 0, prow, h0, &full[slot]);
         } else {
-          tma_load_3d(s.p[0], &tm.m[0], 0, it.hk, row, &full[slot]);
-          tma_load_3d(s.p[1], &tm.m[0], 64, it.hk, row, &full[slot]);
-          tma_load_3d(s.p[2], &tm.m[1], 0, it.hk, row, &full[slot]);
-          tma_load_3d(s.p[3], &tm.m[1], 64, it.hk, row, &full[slot]);
+          tma_load_3d(st, &tm.m[0], 0, row, h0, &full[slot]);
+          tma_load_3d(st + NWC * 2048, &tm.m[0], 64, row, h0, &full[slot]);
+          tma_load_3d(st + 2 * NWC * 2048, &tm.m[1], 0, row, h0, &full[slot]);
+          tma_load_3d(st + 3 * NWC * 2048, &tm.m[1], 64, row, h0, &full[slot]);
         }
       }
     }
     // Every copy this lane issued lands before the CTA may exit.
-    for (uint32_t i = gi > kRing ? gi - kRing : 0; i < gi; ++i) {
-      if (!mbar_wait(&full[i % kRing], (i / kRing) & 1u)) {
+    for (uint32_t i = gs > S ? gs - S : 0; i < gs; ++i) {
+      if (!mbar_wait(&full[i % S], (i / S) & 1u)) {
         set_status(a.status, EXK_S_DRAIN_TIMEOUT);
         break;
       }
@@ -505,17 +537,19 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
     return;
   }
 
-  // -------------------------------------------------- consumers
+  // -------------------------------------------------- consumers: warp = (head hl, page phase ph)
   const int g = lane >> 2, t = lane & 3;
-  const int ctid = threadIdx.x;  // 0 .. NWC*32-1
-  uint32_t gbase = 0;
+  const int hl = warp / WPH, ph = warp % WPH;
+  uint32_t gs = 0;
   bool aborted = false;
   WarpState<NT> st;
   uint32_t qf[NT][16];
 
   for (int item = blockIdx.x; item < a.n_items; item += gridDim.x) {
     const Item it = decode_item(a, item);
-    load_q<NT>(a, it, g, t, qf);
+    const int hk = it.hg * HG + hl;
+    const int nst = (it.npages + WPH - 1) / WPH;
+    load_q<NT>(a, it.b, hk, g, t, qf);
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       st.m[nt][0] = st.m[nt][1] = -INFINITY;
@@ -524,31 +558,33 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
       for (int mm = 0; mm < 8; ++mm) st.acc[nt][mm][0] = st.acc[nt][mm][1] = st.acc[nt][mm][2] = st.acc[nt][mm][3] = 0.f;
     }
     PageMeta pm_next;
-    if (warp < it.npages) pm_next = load_meta<COMP>(a, it, it.page0 + warp);
-    for (int p = warp; p < it.npages; p += NWC) {
+    if (ph < it.npages) pm_next = load_meta<COMP>(a, it.b, hk, it.page0 + ph);
+    for (int s = 0; s < nst; ++s, ++gs) {
+      const int p = s * WPH + ph;  // page of the item this warp takes from the stage
       const PageMeta pm = pm_next;
-      if (p + NWC < it.npages) pm_next = load_meta<COMP>(a, it, it.page0 + p + NWC);
-      const uint32_t gidx = gbase + p;
-      const int slot = gidx % kRing;
+      if (p + WPH < it.npages) pm_next = load_meta<COMP>(a, it.b, hk, it.page0 + p + WPH);
+      const int slot = gs % S;
       if (!aborted) {
         if (*abort_flag) {
           aborted = true;
-        } else if (!mbar_wait(&full[slot], (gidx / kRing) & 1u)) {
+        } else if (!mbar_wait(&full[slot], (gs / S) & 1u)) {
           set_status(a.status, EXK_S_FULL_TIMEOUT);
           *abort_flag = 1;
           aborted = true;
         }
       }
       if (!aborted) {
-        const int vr = min(kP, it.tok1 - (it.page0 + p) * kP);
-        attend_page<COMP, NT>(slot_ptrs<COMP>(ring, slot), pm, vr, a, qf, st, g, t);
+        if (p < it.npages) {
+          const int vr = min(kP, it.tok1 - (it.page0 + p) * kP);
+          attend_page<COMP, NT>(tile_ptrs<COMP, NWC, HG>(ring + slot * C::kStageBytes, hl, ph), pm, vr, a, qf, st,
+                                g, t);
+        }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);
       }
     }
-    gbase += it.npages;
 
-    // ---- merge the consumer warps' states (fixed warp order) and write the split partial
+    // ---- finish the item: full l per head, then (if several page phases) merge them
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -559,50 +595,102 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
         l += __shfl_xor_sync(0xFFFFFFFFu, l, 16);
         st.l[nt][j] = l;
       }
-    named_barrier(1, NWC * 32);
+    const int64_t row0 = static_cast<int64_t>(it.b) * a.Hq + static_cast<int64_t>(hk) * a.G;
+    if constexpr (WPH == 1) {
+      // one warp per head: the warp's state is the split partial
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      const int h0 = nt * 8 + 2 * t;
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int h = nt * 8 + 2 * t + j;
+          if (h < a.G) {
+            const int64_t col = (row0 + h) * a.ns + it.split;
+            if (g == 0) {
+              a.ws_m[col] = st.m[nt][j];
+              a.ws_l[col] = st.l[nt][j];
+            }
+#pragma unroll
+            for (int mm = 0; mm < 8; ++mm) {
+              const int chA = mm < 4 ? 8 * g + 2 * mm : 64 + 8 * g + 2 * (mm - 4);
+              *reinterpret_cast<float2*>(a.ws_o + col * kD + chA) = make_float2(st.acc[nt][mm][j], st.acc[nt][mm][2 + j]);
+            }
+          }
+        }
+    } else {
+      // WPH warps per head, merged in fixed phase order through shared memory
+      named_barrier(1, NWC * 32);  // the previous item's readers are done
       if (g == 0) {
-        mbuf[warp * H8 + h0] = st.m[nt][0];
-        mbuf[warp * H8 + h0 + 1] = st.m[nt][1];
-        lbuf[warp * H8 + h0] = st.l[nt][0];
-        lbuf[warp * H8 + h0 + 1] = st.l[nt][1];
-      }
 #pragma unroll
-      for (int mm = 0; mm < 8; ++mm) {
-        const int chA = mm < 4 ? 8 * g + 2 * mm : 64 + 8 * g + 2 * (mm - 4);
-        float* r = macc + (warp * H8 + h0) * kAccPitch + chA;
-        *reinterpret_cast<float2*>(r) = make_float2(st.acc[nt][mm][0], st.acc[nt][mm][2]);
-        *reinterpret_cast<float2*>(r + kAccPitch) = make_float2(st.acc[nt][mm][1], st.acc[nt][mm][3]);
-      }
-    }
-    named_barrier(1, NWC * 32);
-    for (int e = ctid; e < H8 * 32; e += NWC * 32) {
-      const int h = e >> 5, c4 = (e & 31) * 4;
-      if (h >= a.G) continue;
-      float M = -INFINITY;
+        for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-      for (int w = 0; w < NWC; ++w) M = fmaxf(M, mbuf[w * H8 + h]);
-      float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-      float lsum = 0.f;
-#pragma unroll
-      for (int w = 0; w < NWC; ++w) {
-        const float mw = mbuf[w * H8 + h];
-        const float sc = mw == -INFINITY ? 0.f : ex2(mw - M);
-        const float4 v = *reinterpret_cast<const float4*>(macc + (w * H8 + h) * kAccPitch + c4);
-        o.x += sc * v.x;
-        o.y += sc * v.y;
-        o.z += sc * v.z;
-        o.w += sc * v.w;
-        lsum += sc * lbuf[w * H8 + h];
+          for (int j = 0; j < 2; ++j) {
+            mbuf[warp * H8 + nt * 8 + 2 * t + j] = st.m[nt][j];
+            lbuf[warp * H8 + nt * 8 + 2 * t + j] = st.l[nt][j];
+          }
       }
-      const int64_t row = static_cast<int64_t>(it.b) * a.Hq + it.hk * a.G + h;
-      const int64_t col = row * a.ns + it.split;
-      *reinterpret_cast<float4*>(a.ws_o + col * kD + c4) = o;
-      if (c4 == 0) {
-        a.ws_m[col] = M;
-        a.ws_l[col] = lsum;
+      named_barrier(1, NWC * 32);
+      float scale[NT][2];
+      float lsum[NT][2];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int h = nt * 8 + 2 * t + j;
+          float M = -INFINITY;
+#pragma unroll
+          for (int q2 = 0; q2 < WPH; ++q2) M = fmaxf(M, mbuf[(hl * WPH + q2) * H8 + h]);
+          const float mw = st.m[nt][j];
+          scale[nt][j] = mw == -INFINITY ? 0.f : ex2(mw - M);
+          float L = 0.f;
+#pragma unroll
+          for (int q2 = 0; q2 < WPH; ++q2) {
+            const float m2 = mbuf[(hl * WPH + q2) * H8 + h];
+            L += (m2 == -INFINITY ? 0.f : ex2(m2 - M)) * lbuf[(hl * WPH + q2) * H8 + h];
+          }
+          lsum[nt][j] = L;
+          if (ph == 0) st.m[nt][j] = M;
+        }
+      float* buf = macc + hl * H8 * kAccPitch;
+#pragma unroll 1
+      for (int q2 = 0; q2 < WPH; ++q2) {
+        if (ph == q2) {
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int mm = 0; mm < 8; ++mm) {
+              const int chA = mm < 4 ? 8 * g + 2 * mm : 64 + 8 * g + 2 * (mm - 4);
+#pragma unroll
+              for (int j = 0; j < 2; ++j) {
+                float* r = buf + (nt * 8 + 2 * t + j) * kAccPitch + chA;
+                float2 v = make_float2(scale[nt][j] * st.acc[nt][mm][j], scale[nt][j] * st.acc[nt][mm][2 + j]);
+                if (q2 > 0) {
+                  const float2 o = *reinterpret_cast<const float2*>(r);
+                  v.x += o.x;
+                  v.y += o.y;
+                }
+                if (q2 == WPH - 1) {
+                  const int h = nt * 8 + 2 * t + j;
+                  if (h < a.G) *reinterpret_cast<float2*>(a.ws_o + ((row0 + h) * a.ns + it.split) * kD + chA) = v;
+                } else {
+                  *reinterpret_cast<float2*>(r) = v;
+                }
+              }
+            }
+        }
+        if (q2 < WPH - 1) named_barrier(1, NWC * 32);
+      }
+      if (ph == 0 && g == 0) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int h = nt * 8 + 2 * t + j;
+            if (h < a.G) {
+              const int64_t col = (row0 + h) * a.ns + it.split;
+              a.ws_m[col] = st.m[nt][j];
+              a.ws_l[col] = lsum[nt][j];
+            }
+          }
       }
     }
   }
@@ -637,32 +725,49 @@ __global__ void __launch_bounds__(128) merge_kernel(const float* __restrict__ o,
   reinterpret_cast<uint2*>(out + static_cast<int64_t>(row) * kD)[lane] = r;
 }
 
+
 // ------------------------------------------------------------------ host side
 
 namespace {
 
-template <bool COMP, int NT, int NWC>
+template <bool COMP, int NT, int NWC, int HG>
 int launch_split(const AttnArgs& a, const AttnMaps& maps, int grid, int device, cudaStream_t stream) {
-  using L = Smem<COMP, NT, NWC>;
+  using C = Cfg<COMP, NT, NWC, HG>;
   static bool configured[64] = {};
-  auto kern = attn_split_kernel<COMP, NT, NWC>;
+  auto kern = attn_split_kernel<COMP, NT, NWC, HG>;
   if (!configured[device]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kBytes);
     if (e != cudaSuccess) return static_cast<int>(e);
     configured[device] = true;
   }
-  kern<<<grid, (NWC + 1) * 32, L::kBytes, stream>>>(a, maps);
+  kern<<<grid, (NWC + 1) * 32, C::kBytes, stream>>>(a, maps);
   return launch_status();
 }
 
-template <bool COMP>
-int dispatch_split(const AttnArgs& a, const AttnMaps& maps, int grid, int nwc, int device, cudaStream_t stream) {
-  const bool two = a.G > 8;
-  if (nwc == 4) return two ? launch_split<COMP, 2, 4>(a, maps, grid, device, stream)
-                           : launch_split<COMP, 1, 4>(a, maps, grid, device, stream);
-  return two ? launch_split<COMP, 2, 8>(a, maps, grid, device, stream)
-             : launch_split<COMP, 1, 8>(a, maps, grid, device, stream);
+template <bool COMP, int NT, int NWC>
+int by_group(const AttnArgs& a, const AttnMaps& maps, int hg, int grid, int device, cudaStream_t stream) {
+  switch (hg) {
+    case 1: return launch_split<COMP, NT, NWC, 1>(a, maps, grid, device, stream);
+    case 2: return launch_split<COMP, NT, NWC, 2>(a, maps, grid, device, stream);
+    case 4: return launch_split<COMP, NT, NWC, 4>(a, maps, grid, device, stream);
+    default:
+      if constexpr (NWC >= 8) return launch_split<COMP, NT, NWC, 8>(a, maps, grid, device, stream);
+      return EXK_EARG;
+  }
 }
+
+template <bool COMP>
+int dispatch_split(const AttnArgs& a, const AttnMaps& maps, int hg, int grid, int nwc, int device,
+                   cudaStream_t stream) {
+  const bool two = a.G > 8;
+  if (nwc == 4) return two ? by_group<COMP, 2, 4>(a, maps, hg, grid, device, stream)
+                           : by_group<COMP, 1, 4>(a, maps, hg, grid, device, stream);
+  return two ? by_group<COMP, 2, 8>(a, maps, hg, grid, device, stream)
+             : by_group<COMP, 1, 8>(a, maps, hg, grid, device, stream);
+}
+
+// Heads per CTA actually used: the plan's head group, capped by the consumer warps.
+int cta_heads(int hkv, int nwc) { return std::min(head_group(hkv), nwc); }
 
 // Validates the shapes shared by both split kernels and fills AttnArgs.
 int common_args(AttnArgs& a, const uint16_t* q, int B, int TS, int Hkv, int Hq, int T, int s0, int s1,
@@ -695,8 +800,9 @@ int common_args(AttnArgs& a, const uint16_t* q, int B, int TS, int Hkv, int Hq, 
   a.s0 = s0;
   // splits entirely past T (possible when s1 > the plan's last split) hold no work
   const int last = (T - 1) / ws->split_len;
-  a.nsl = min(s1, last + 1) - s0;
-  const int64_t items = static_cast<int64_t>(B) * Hkv * a.nsl;
+  a.nsl = std::min(s1, last + 1) - s0;
+  a.ngroups = Hkv / cta_heads(Hkv, nwc);
+  const int64_t items = static_cast<int64_t>(B) * a.ngroups * a.nsl;
   if (items > (int64_t{1} << 30)) return EXK_EARG;
   a.n_items = static_cast<int>(items);
   a.qk_scale = qk_scale;
@@ -709,6 +815,16 @@ int common_args(AttnArgs& a, const uint16_t* q, int B, int TS, int Hkv, int Hq, 
   return 0;
 }
 
+// Tensor map over a [B*TS rows, H heads, width] buffer, addressed as
+// (channel byte/element, token row, head): dims ordered so that a box of
+// (width, rows, heads) lands head-major in shared memory ([heads][rows][width]).
+int head_major_map(CUtensorMap* m, CUtensorMapDataType dt, const void* ptr, int width, int elem_bytes, int64_t rows,
+                   int H, int box_w, int box_rows, int box_heads, CUtensorMapSwizzle sw) {
+  const uint64_t row_stride = static_cast<uint64_t>(width) * elem_bytes * H;
+  const uint64_t head_stride = static_cast<uint64_t>(width) * elem_bytes;
+  return make_tmap_3d(m, dt, ptr, width, rows, H, row_stride, head_stride, box_w, box_rows, box_heads, sw);
+}
+
 }  // namespace
 
 }  // namespace exk
@@ -717,23 +833,28 @@ using namespace exk;
 
 extern "C" int exk_plan_splits(int B, int Hkv, int T, int num_ctas, int32_t* ns_out, int32_t* sl_out) {
   if (B <= 0 || Hkv <= 0 || T <= 0 || num_ctas <= 0 || ns_out == nullptr || sl_out == nullptr) return EXK_EARG;
-  // Cost of a candidate = (items on the busiest CTA) x (pages per item + fixed
-  // per-item overhead of ~2 pages: Q load, pipeline refill, epilogue merge).
+  // Items are (sequence, head group of up to 8 heads, split); a CTA's 8 consumer
+  // warps take WPH = 8 / group pages of the group per stage. Cost of a
+  // candidate = (items on the busiest CTA) x (stages per item + a fixed
+  // per-item overhead of ~2 stages: Q load, pipeline refill, epilogue).
+  const int64_t hg = head_group(Hkv);
+  const int64_t wph = 8 / hg;
   const int64_t npt = (T + kP - 1) / kP;
-  const int64_t bh = static_cast<int64_t>(B) * Hkv;
-  constexpr int64_t kItemOverheadPages = 2;
+  const int64_t units = static_cast<int64_t>(B) * (Hkv / hg);
+  constexpr int64_t kItemOverhead = 2;
   const int64_t nmax = std::min<int64_t>(npt, std::max<int64_t>(1, 8 * static_cast<int64_t>(num_ctas)));
   int64_t best_cost = -1, best_spp = npt;
   int64_t prev_spp = -1;
   for (int64_t n = 1; n <= nmax; ++n) {
-    const int64_t spp = (npt + n - 1) / n;
+    int64_t spp = (npt + n - 1) / n;
+    spp = (spp + wph - 1) / wph * wph;  // whole stages per split
     if (spp == prev_spp) continue;
     prev_spp = spp;
     const int64_t nsr = (npt + spp - 1) / spp;
     if (nsr > 4096) break;
-    const int64_t items = bh * nsr;
+    const int64_t items = units * nsr;
     const int64_t waves = (items + num_ctas - 1) / num_ctas;
-    const int64_t cost = waves * (spp + kItemOverheadPages);
+    const int64_t cost = waves * (spp / wph + kItemOverhead);
     if (best_cost < 0 || cost < best_cost) {
       best_cost = cost;
       best_spp = spp;
@@ -754,8 +875,11 @@ extern "C" int exk_attn_split_compressed(const uint16_t* q, const exk_cview* k, 
   if (r != 0) return r;
   int sms = 0;
   if ((r = use_device(device, &sms)) != 0) return r;
+  const int hg = cta_heads(Hkv, consumer_warps);
+  const int wph = consumer_warps / hg;
   const exk_cview* cv[2] = {k, v};
   AttnMaps maps;
+  const int64_t rows = static_cast<int64_t>(B) * TS, prows = static_cast<int64_t>(B) * (TS / kP);
   for (int i = 0; i < 2; ++i) {
     const exk_cview* c = cv[i];
     if (!aligned16(c->sm) || !aligned16(c->code) || !aligned16(c->base) || !aligned16(c->raw)) return EXK_EALIGN;
@@ -764,19 +888,18 @@ extern "C" int exk_attn_split_compressed(const uint16_t* q, const exk_cview* k, 
     a.rowoff[i] = c->rowoff;
     a.raw[i] = c->raw;
     a.raw_rows[i] = c->raw_rows;
-    const uint64_t rows = static_cast<uint64_t>(B) * TS, prows = static_cast<uint64_t>(B) * (TS / kP);
-    if ((r = make_tmap_3d(&maps.m[3 * i + 0], CU_TENSOR_MAP_DATA_TYPE_UINT8, c->sm, 128, Hkv, rows, 128,
-                          128ull * Hkv, 128, 1, kP, CU_TENSOR_MAP_SWIZZLE_128B)) != 0)
+    if ((r = head_major_map(&maps.m[3 * i + 0], CU_TENSOR_MAP_DATA_TYPE_UINT8, c->sm, 128, 1, rows, Hkv, 128,
+                            kP * wph, hg, CU_TENSOR_MAP_SWIZZLE_128B)) != 0)
       return r;
-    if ((r = make_tmap_3d(&maps.m[3 * i + 1], CU_TENSOR_MAP_DATA_TYPE_UINT8, c->code, 64, Hkv, rows, 64,
-                          64ull * Hkv, 64, 1, kP, CU_TENSOR_MAP_SWIZZLE_64B)) != 0)
+    if ((r = head_major_map(&maps.m[3 * i + 1], CU_TENSOR_MAP_DATA_TYPE_UINT8, c->code, 64, 1, rows, Hkv, 64,
+                            kP * wph, hg, CU_TENSOR_MAP_SWIZZLE_64B)) != 0)
       return r;
-    if ((r = make_tmap_3d(&maps.m[3 * i + 2], CU_TENSOR_MAP_DATA_TYPE_UINT8, c->base, 128, Hkv, prows, 128,
-                          128ull * Hkv, 128, 1, 1, CU_TENSOR_MAP_SWIZZLE_NONE)) != 0)
+    if ((r = head_major_map(&maps.m[3 * i + 2], CU_TENSOR_MAP_DATA_TYPE_UINT8, c->base, 128, 1, prows, Hkv, 128,
+                            wph, hg, CU_TENSOR_MAP_SWIZZLE_NONE)) != 0)
       return r;
   }
   const int grid = static_cast<int>(std::min<int64_t>(a.n_items, sms));
-  return dispatch_split<true>(a, maps, grid, consumer_warps, device, static_cast<cudaStream_t>(stream));
+  return dispatch_split<true>(a, maps, hg, grid, consumer_warps, device, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int exk_attn_split_bf16(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int TS, int Hkv,
@@ -789,16 +912,18 @@ extern "C" int exk_attn_split_bf16(const uint16_t* q, const uint16_t* k, const u
   int sms = 0;
   if ((r = use_device(device, &sms)) != 0) return r;
   if (!aligned16(k) || !aligned16(v)) return EXK_EALIGN;
+  const int hg = cta_heads(Hkv, consumer_warps);
+  const int wph = consumer_warps / hg;
   AttnMaps maps;
-  const uint64_t rows = static_cast<uint64_t>(B) * TS;
-  if ((r = make_tmap_3d(&maps.m[0], CU_TENSOR_MAP_DATA_TYPE_UINT16, k, 128, Hkv, rows, 256, 256ull * Hkv, 64, 1, kP,
-                        CU_TENSOR_MAP_SWIZZLE_128B)) != 0)
+  const int64_t rows = static_cast<int64_t>(B) * TS;
+  if ((r = head_major_map(&maps.m[0], CU_TENSOR_MAP_DATA_TYPE_UINT16, k, 128, 2, rows, Hkv, 64, kP * wph, hg,
+                          CU_TENSOR_MAP_SWIZZLE_128B)) != 0)
     return r;
-  if ((r = make_tmap_3d(&maps.m[1], CU_TENSOR_MAP_DATA_TYPE_UINT16, v, 128, Hkv, rows, 256, 256ull * Hkv, 64, 1, kP,
-                        CU_TENSOR_MAP_SWIZZLE_128B)) != 0)
+  if ((r = head_major_map(&maps.m[1], CU_TENSOR_MAP_DATA_TYPE_UINT16, v, 128, 2, rows, Hkv, 64, kP * wph, hg,
+                          CU_TENSOR_MAP_SWIZZLE_128B)) != 0)
     return r;
   const int grid = static_cast<int>(std::min<int64_t>(a.n_items, sms));
-  return dispatch_split<false>(a, maps, grid, consumer_warps, device, static_cast<cudaStream_t>(stream));
+  return dispatch_split<false>(a, maps, hg, grid, consumer_warps, device, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int exk_attn_merge(const exk_partials* ws, int rows, uint16_t* out, int device, void* stream) {

@@ -75,6 +75,7 @@ extern "C" const char* exk_error_string(int code) {
     case EXK_ETMAP: return "exactkv_b200: cuTensorMapEncodeTiled rejected a tensor map";
     case EXK_EDRIVER: return "exactkv_b200: cuTensorMapEncodeTiled entry point unavailable";
     case EXK_EHEADS: return "exactkv_b200: more than 16 query heads per KV head";
+    case EXK_ESCRATCH: return "exactkv_b200: split partials exceed the fixed scratch of exk_attention_compressed_noalloc";
     default: break;
   }
   if (code > 0) return cudaGetErrorString(static_cast<cudaError_t>(code));

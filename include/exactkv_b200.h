@@ -43,6 +43,7 @@ extern "C" {
 #define EXK_ETMAP     (-3)  /* cuTensorMapEncodeTiled rejected a tensor map */
 #define EXK_EDRIVER   (-4)  /* the driver entry point could not be resolved */
 #define EXK_EHEADS    (-5)  /* more than 16 query heads per KV head */
+#define EXK_ESCRATCH  (-6)  /* partials larger than EXK_NOALLOC_SCRATCH_BYTES */
 
 /* device status codes (written to the caller's int32 status word) */
 #define EXK_S_OK             0
@@ -127,6 +128,23 @@ int exk_encode_pages(const uint16_t *src, int64_t s_b, int64_t s_pg, int64_t s_p
  * decoder. Replaces _dec_only_kernel/decode_to_bf16 (exactkv/kernels.py:197-211, 331-337). */
 int exk_decode_to_bf16(const exk_cview *c, int B, int TS, int H, int T, uint16_t *out,
                        int32_t *status, int device, void *stream);
+
+/* Split-K decode attention over the compressed cache that allocates nothing
+ * and takes no workspace: the split partials live in a fixed device array of
+ * EXK_NOALLOC_SCRATCH_BYTES inside the library, which every GPU that loads the
+ * library holds until the process exits. For callers that cannot allocate
+ * device memory when they call (a runtime with a fixed memory plan, a plugin
+ * whose enqueue must not call cudaMalloc). Same arguments and result as
+ * exk_attn_split_compressed over the full plan followed by exk_attn_merge into
+ * out [B*Hq, 128]. Returns EXK_ESCRATCH when B*Hq x splits x 130 fp32 exceed
+ * the array. The first call on a device looks up the array's device address
+ * (make it before any stream capture). All calls on a GPU share the array:
+ * calls that overlap on the GPU race. No counterpart in the reference. */
+#define EXK_NOALLOC_SCRATCH_BYTES (4u << 20)
+int exk_attention_compressed_noalloc(const uint16_t *q, const exk_cview *k, const exk_cview *v,
+                                     int B, int TS, int Hkv, int Hq, int T, int consumer_warps,
+                                     float qk_scale, uint16_t *out, int32_t *status, int device,
+                                     void *stream);
 
 /* Human-readable text for a return value or a device status code. */
 const char *exk_error_string(int code);

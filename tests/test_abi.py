@@ -66,8 +66,8 @@ def test_plan_covers_tokens_in_pages(B, Hkv, T):
 
 
 def test_plan_balances_llama_shape():
-    # 32 x 4096, 8 KV heads over 148 SMs: 4 splits of 1024 -> 1024 items, 7 waves of 6.9 average
-    assert _plan(32, 8, 4096, 148) == (4, 1024)
+    # 32 x 4096, 8 KV heads (one head group) over 148 SMs: 9 splits of 29 pages -> 288 items, 2 waves
+    assert _plan(32, 8, 4096, 148) == (9, 464)
 
 
 def test_plan_rejects_bad_arguments():
