@@ -284,6 +284,8 @@ def run_ours(a, rank, world, local):
     achieved_gbs = nbytes / (split_us * 1e-6) / 1e9       # all algorithmic bytes are the split kernel's
     traffic = profiled_traffic()
 
+    encoder = None if a.quick else time_encoder(kbf, B, T, Hkv, dev)
+
     e2e = None
     if not (a.no_e2e or a.quick):
         e2e = run_e2e(a, kc, vc, B, Hq, Hkv, T, dev, world, raw_rows, ns)
@@ -312,6 +314,7 @@ def run_ours(a, rank, world, local):
                      "frac": round(achieved_gbs / peak, 4), "peak_source": f"{peak_src} hbm_gbs (copy, read+write)",
                      "traffic": traffic, "kernel": "exk::attn_split_kernel<compressed>"},
         "gpu_launches": 2 * a.steps,
+        "encoder": encoder,
         "clocks": clocks.summary(),
         "e2e": e2e,
         "cpu_baseline": cpu,
@@ -321,6 +324,35 @@ def run_ours(a, rank, world, local):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def time_encoder(kbf, B, T, Hkv, dev, reps=5):
+    """The page encoder over the whole batch's keys in one encode_pages call (a
+    prefill of B sequences): bf16 bytes read and compressed bytes written per us."""
+    import torch
+
+    import exactkv_b200 as ekv
+    from exactkv_b200 import kernels
+    c = ekv.CompressedKV(B, T, Hkv, 128, device=dev, reserve=0.05)
+    src = kbf[:, :T]
+    st = (src.stride(0), 16 * src.stride(1), src.stride(1), src.stride(2))
+    times = []
+    for i in range(reps + 2):
+        c.cnt.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        kernels.encode_pages(src, st, c._buf(), 0, 0, B, T // 16)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        if i >= 2:
+            times.append(e0.elapsed_time(e1) * 1e3)
+    n = int(c.cnt.item())
+    us = statistics.median(times)
+    rows = B * T * Hkv
+    written = rows * 192 + (rows // 16) * 136 + n * 256
+    return {"us": round(us, 2), "bf16_read_gbs": round(rows * 256 / us / 1e3, 1),
+            "compressed_written_gbs": round(written / us / 1e3, 1), "raw_rows": n,
+            "what": f"encode_pages over {B} x {T} tokens x {Hkv} heads of keys (3 launches: encode, slot scan, raw copy)"}
 
 
 def run_e2e(a, kc, vc, B, Hq, Hkv, T0, dev, world, raw_rows0, ns0):

@@ -33,7 +33,6 @@ class CompressedKV:
         self.rowoff = torch.zeros(B, NP, H, **i32)
         self.cnt = torch.zeros(1, **i32)        # raw-pool rows taken (may exceed cap: overflow)
         self._before = torch.zeros(1, **i32)    # counter before the last encoded page
-        self._chain = torch.zeros(2, **i32)     # encoder scratch (left zeroed by every launch)
         self.cap = max(64, int(B * TS * H * reserve))
         self.raw = torch.zeros(self.cap + B * H * P, D, dtype=torch.bfloat16, device=device)
         self.T = 0
@@ -65,7 +64,7 @@ class CompressedKV:
 
     def _buf(self):
         return dict(sm=self.sm, code=self.code, base=self.base, rowmask=self.rowmask, rowoff=self.rowoff,
-                    raw=self.raw, cnt=self.cnt, cap=self.cap, TS=self.TS, H=self.H, D=self.D, chain=self._chain)
+                    raw=self.raw, cnt=self.cnt, cap=self.cap, TS=self.TS, H=self.H, D=self.D)
 
     def _grow(self, need):
         new_cap = max(2 * self.cap, need + self.cap // 4)

@@ -34,7 +34,7 @@ def encode_reference(x):
     buf = dict(sm=torch.empty(B, T, H, D, **u8), code=torch.empty(B, T, H, D // 2, **u8),
                base=torch.empty(B, NP, H, D, **u8), rowmask=torch.empty(B, NP, H, **i32),
                rowoff=torch.empty(B, NP, H, **i32), raw=torch.empty(B * T * H, D, dtype=torch.bfloat16, device=dev),
-               cnt=torch.zeros(1, **i32), chain=torch.zeros(2, **i32), cap=B * T * H, TS=T, H=H, D=D)
+               cnt=torch.zeros(1, **i32), cap=B * T * H, TS=T, H=H, D=D)
     kernels.encode_pages(x, (x.stride(0), P * x.stride(1), x.stride(1), x.stride(2)), buf, 0, 0, B, NP)
     n = int(buf["cnt"].item())
     return dict(shape=(B, T, H, D), sm=buf["sm"], code=buf["code"], base=buf["base"], rowmask=buf["rowmask"],

@@ -4,14 +4,14 @@
 // channels. Lane (q = lane%16, th = lane/16) holds channels 4q..4q+3 and
 // 64+4q..64+4q+3 of tokens 8th..8th+7, so a channel's 16 exponents live in
 // lanes q and q+16 and one shuffle completes every per-channel reduction.
-// Raw-pool slots: the CTAs of a launch take tickets in start order; CTA k
-// covers page-heads [8k, 8k+8), and after its pages are encoded it waits
-// (bounded) for CTA k-1 to publish the running pool count, takes its range and
-// publishes the next. The slots therefore follow (sequence, page, head) order
-// exactly as the reference's encode_reference writes them
-// (exactkv/codec.py:49-53), independent of scheduling, while the pool
-// counter still advances by one atomic-equivalent step per CTA
-// (exactkv/kernels.py:261-268 uses one atomic_add per page-head).
+// Raw-pool slots are assigned in (sequence, page, head) order — the order the
+// reference's encode_reference writes them (exactkv/codec.py:49-53) — in three
+// launches that never wait on one another: encode_kernel writes sm, code, base
+// and rowmask; raw_offsets_kernel (one CTA) scans the pages' raw-row counts
+// from the pool counter, writes rowoff and advances the counter;
+// raw_copy_kernel copies every escaped row from the source into its slot.
+// The reference takes a slot range with one atomic_add per page-head
+// (exactkv/kernels.py:261-268), whose order depends on scheduling.
 #include <algorithm>
 
 #include "exk_device.cuh"
@@ -20,6 +20,7 @@
 namespace exk {
 
 constexpr int kEncWarps = 8;
+constexpr int kScanThreads = 1024;
 
 struct EncArgs {
   const uint16_t* src;
@@ -32,20 +33,17 @@ struct EncArgs {
   uint16_t* raw;
   int64_t raw_cap;
   int32_t* cnt;
-  int32_t* chain;   // [0] ticket counter, [1] number of CTAs that published
-  int32_t* status;
   int b0, pg0, nb, npg, H, TS, NP;
-  int n_ph, n_cta;
+  int n_ph;
 };
 
-__device__ __forceinline__ int ld_acquire(const int32_t* p) {
-  int v;
-  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void st_release(int32_t* p, int v) {
-  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// Page-head ph of a launch (ordered sequence, page, head) -> its index in the
+// [B, TS/16, H] page arrays, and its source offset in elements.
+__device__ __forceinline__ int64_t page_index(const EncArgs& a, int ph, int& bi, int& pg, int& hk) {
+  hk = ph % a.H;
+  pg = (ph / a.H) % a.npg;
+  bi = ph / (a.H * a.npg);
+  return (static_cast<int64_t>(a.b0 + bi) * a.NP + a.pg0 + pg) * a.H + hk;
 }
 
 __device__ __forceinline__ uint32_t half_of(const uint32_t (&w)[4], int c) {
@@ -54,169 +52,180 @@ __device__ __forceinline__ uint32_t half_of(const uint32_t (&w)[4], int c) {
 }
 
 template <bool VEC>
+__device__ __forceinline__ void load_row_quads(const uint16_t* p, int q, uint32_t (&v)[4]) {
+  if constexpr (VEC) {
+    const uint2 lo = *reinterpret_cast<const uint2*>(p + 4 * q);
+    const uint2 hi = *reinterpret_cast<const uint2*>(p + 64 + 4 * q);
+    v[0] = lo.x; v[1] = lo.y; v[2] = hi.x; v[3] = hi.y;
+  } else {
+    v[0] = p[4 * q] | (uint32_t(p[4 * q + 1]) << 16);
+    v[1] = p[4 * q + 2] | (uint32_t(p[4 * q + 3]) << 16);
+    v[2] = p[64 + 4 * q] | (uint32_t(p[64 + 4 * q + 1]) << 16);
+    v[3] = p[64 + 4 * q + 2] | (uint32_t(p[64 + 4 * q + 3]) << 16);
+  }
+}
+
+template <bool VEC>
 __global__ void __launch_bounds__(kEncWarps * 32) encode_kernel(const __grid_constant__ EncArgs a) {
-  __shared__ int s_ticket, s_base;
-  __shared__ int s_cnt[kEncWarps];
-  if (threadIdx.x == 0) s_ticket = atomicAdd(&a.chain[0], 1);
-  __syncthreads();
-  const int tk = s_ticket;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int ph = tk * kEncWarps + warp;
-  const bool active = ph < a.n_ph;  // uniform per warp
+  const int ph = blockIdx.x * kEncWarps + warp;
+  if (ph >= a.n_ph) return;  // whole warp
   const int q = lane & 15, th = lane >> 4;
+  int bi, pg, hk;
+  const int64_t page = page_index(a, ph, bi, pg, hk);
 
-  int hk = 0, pg = 0, bi = 0;
   uint32_t v[8][4];  // [token][word]: bf16 pairs (4q,4q+1), (4q+2,4q+3), (64+4q, ..), (64+4q+2, ..)
-  uint32_t rm = 0;
-  if (active) {
-    hk = ph % a.H;
-    pg = (ph / a.H) % a.npg;
-    bi = ph / (a.H * a.npg);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const uint16_t* p = a.src + bi * a.s_b + pg * a.s_pg + static_cast<int64_t>(th * 8 + i) * a.s_p + hk * a.s_h;
-      if constexpr (VEC) {
-        const uint2 lo = *reinterpret_cast<const uint2*>(p + 4 * q);
-        const uint2 hi = *reinterpret_cast<const uint2*>(p + 64 + 4 * q);
-        v[i][0] = lo.x; v[i][1] = lo.y; v[i][2] = hi.x; v[i][3] = hi.y;
-      } else {
-        v[i][0] = p[4 * q] | (uint32_t(p[4 * q + 1]) << 16);
-        v[i][1] = p[4 * q + 2] | (uint32_t(p[4 * q + 3]) << 16);
-        v[i][2] = p[64 + 4 * q] | (uint32_t(p[64 + 4 * q + 1]) << 16);
-        v[i][3] = p[64 + 4 * q + 2] | (uint32_t(p[64 + 4 * q + 3]) << 16);
-      }
-    }
-    // per-channel maximum exponent and zero presence over the 16 tokens
-    int emax[8];
-    uint32_t has0 = 0;
+  for (int i = 0; i < 8; ++i)
+    load_row_quads<VEC>(a.src + bi * a.s_b + pg * a.s_pg + static_cast<int64_t>(th * 8 + i) * a.s_p + hk * a.s_h,
+                        q, v[i]);
+  // per-channel maximum exponent and zero presence over the 16 tokens
+  int emax[8];
+  uint32_t has0 = 0;
 #pragma unroll
-    for (int c = 0; c < 8; ++c) emax[c] = 0;
+  for (int c = 0; c < 8; ++c) emax[c] = 0;
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const int e = (half_of(v[i], c) >> 7) & 0xFF;
-        emax[c] = max(emax[c], e);
-        has0 |= (e == 0 ? 1u : 0u) << c;
-      }
-#pragma unroll
-    for (int c = 0; c < 8; ++c) emax[c] = max(emax[c], __shfl_xor_sync(0xFFFFFFFFu, emax[c], 16));
-    has0 |= __shfl_xor_sync(0xFFFFFFFFu, has0, 16);
-
-    int bse[8];
-    bool zm[8];
-    uint32_t bw[2] = {0u, 0u};
+  for (int i = 0; i < 8; ++i)
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
-      bse[c] = max(emax[c] - 15, 0);
-      zm[c] = ((has0 >> c) & 1u) && bse[c] > 0;  // a zero the plain 15-step window cannot hold
-      const int byte = min(zm[c] ? bse[c] + 128 : bse[c], 255);
-      bw[c >> 2] |= uint32_t(byte) << (8 * (c & 3));
+      const int e = (half_of(v[i], c) >> 7) & 0xFF;
+      emax[c] = max(emax[c], e);
+      has0 |= (e == 0 ? 1u : 0u) << c;
     }
+#pragma unroll
+  for (int c = 0; c < 8; ++c) emax[c] = max(emax[c], __shfl_xor_sync(0xFFFFFFFFu, emax[c], 16));
+  has0 |= __shfl_xor_sync(0xFFFFFFFFu, has0, 16);
 
-    const int64_t page = (static_cast<int64_t>(a.b0 + bi) * a.NP + a.pg0 + pg) * a.H + hk;
-    uint32_t escrow = 0;
+  int bse[8];
+  bool zm[8];
+  uint32_t bw[2] = {0u, 0u};
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int tok = th * 8 + i;
-      const int64_t row = (static_cast<int64_t>(a.b0 + bi) * a.TS + (a.pg0 + pg) * kP + tok) * a.H + hk;
-      uint32_t smw[2] = {0u, 0u}, cw = 0u;
-      bool esc = false;
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const uint32_t u = half_of(v[i], c);
-        const int e = (u >> 7) & 0xFF;
-        const bool zero = zm[c] && e == 0;
-        int code = zero ? 0 : e - bse[c];
-        const int lo = zm[c] ? 1 : 0;
-        esc |= (code < lo && !zero) || bse[c] >= 128;
-        code = min(max(code, 0), 15);
-        smw[c >> 2] |= (((u >> 8) & 0x80u) | (u & 0x7Fu)) << (8 * (c & 3));
-        cw |= uint32_t(code) << (8 * (c & 3) + 4 * (c >> 2));
-      }
-      *reinterpret_cast<uint32_t*>(a.sm + row * kD + 4 * q) = smw[0];
-      *reinterpret_cast<uint32_t*>(a.sm + row * kD + 64 + 4 * q) = smw[1];
-      *reinterpret_cast<uint32_t*>(a.code + row * (kD / 2) + 4 * q) = cw;
-      escrow |= (esc ? 1u : 0u) << i;
-    }
-    if (th == 0) {
-      *reinterpret_cast<uint32_t*>(a.base + page * kD + 4 * q) = bw[0];
-      *reinterpret_cast<uint32_t*>(a.base + page * kD + 64 + 4 * q) = bw[1];
-    }
-    // rowmask: token 8th+i escapes if any of its 16 lanes saw an escape
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const uint32_t bal = __ballot_sync(0xFFFFFFFFu, (escrow >> i) & 1u);
-      rm |= ((bal & 0xFFFFu) ? 1u : 0u) << i;
-      rm |= ((bal >> 16) ? 1u : 0u) << (8 + i);
-    }
+  for (int c = 0; c < 8; ++c) {
+    bse[c] = max(emax[c] - 15, 0);
+    zm[c] = ((has0 >> c) & 1u) && bse[c] > 0;  // a zero the plain 15-step window cannot hold
+    const int byte = min(zm[c] ? bse[c] + 128 : bse[c], 255);
+    bw[c >> 2] |= uint32_t(byte) << (8 * (c & 3));
   }
-  if (lane == 0) s_cnt[warp] = active ? __popc(rm) : 0;
-  __syncthreads();
 
-  if (threadIdx.x == 0) {
-    int total = 0;
-    for (int w = 0; w < kEncWarps; ++w) {
-      const int c = s_cnt[w];
-      s_cnt[w] = total;
-      total += c;
-    }
-    bool ok = true;
-    if (tk > 0) {
-      uint64_t t0 = 0;
-      for (int it = 0; ld_acquire(&a.chain[1]) != tk; ++it) {
-        if (it < 32) continue;
-        if (t0 == 0) t0 = globaltimer();
-        if (*reinterpret_cast<volatile int32_t*>(a.status) != 0 || globaltimer() - t0 > kWaitLimitNs) {
-          set_status(a.status, EXK_S_CHAIN_TIMEOUT);
-          ok = false;
-          break;
-        }
-        __nanosleep(64);
-      }
-    }
-    volatile int32_t* cnt = a.cnt;
-    const int base_off = *cnt;
-    *cnt = base_off + total;
-    __threadfence();
-    st_release(&a.chain[1], tk + 1);
-    if (tk == a.n_cta - 1) {
-      // every other CTA has taken its ticket and published: leave the chain zeroed
-      a.chain[0] = 0;
-      a.chain[1] = 0;
-    }
-    s_base = ok ? base_off : -1;
-  }
-  __syncthreads();
-
-  if (active) {
-    const int base_off = s_base;
-    const int64_t page = (static_cast<int64_t>(a.b0 + bi) * a.NP + a.pg0 + pg) * a.H + hk;
-    const int off = base_off < 0 ? 0 : base_off + s_cnt[warp];
-    if (lane == 0) {
-      a.rowmask[page] = static_cast<int32_t>(rm);
-      a.rowoff[page] = off;
-    }
-    if (base_off >= 0) {
+  uint32_t escrow = 0;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int tok = th * 8 + i;
-        if ((rm >> tok) & 1u) {
-          const int64_t ridx = static_cast<int64_t>(off) + __popc(rm & ((1u << tok) - 1u));
-          if (ridx < a.raw_cap) {
-            uint16_t* d = a.raw + ridx * kD;
-            if constexpr (VEC) {
-              *reinterpret_cast<uint2*>(d + 4 * q) = make_uint2(v[i][0], v[i][1]);
-              *reinterpret_cast<uint2*>(d + 64 + 4 * q) = make_uint2(v[i][2], v[i][3]);
-            } else {
-              *reinterpret_cast<uint32_t*>(d + 4 * q) = v[i][0];
-              *reinterpret_cast<uint32_t*>(d + 4 * q + 2) = v[i][1];
-              *reinterpret_cast<uint32_t*>(d + 64 + 4 * q) = v[i][2];
-              *reinterpret_cast<uint32_t*>(d + 64 + 4 * q + 2) = v[i][3];
-            }
-          }
-        }
+  for (int i = 0; i < 8; ++i) {
+    const int tok = th * 8 + i;
+    const int64_t row = (static_cast<int64_t>(a.b0 + bi) * a.TS + (a.pg0 + pg) * kP + tok) * a.H + hk;
+    uint32_t smw[2] = {0u, 0u}, cw = 0u;
+    bool esc = false;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const uint32_t u = half_of(v[i], c);
+      const int e = (u >> 7) & 0xFF;
+      const bool zero = zm[c] && e == 0;
+      int code = zero ? 0 : e - bse[c];
+      const int lo = zm[c] ? 1 : 0;
+      esc |= (code < lo && !zero) || bse[c] >= 128;
+      code = min(max(code, 0), 15);
+      smw[c >> 2] |= (((u >> 8) & 0x80u) | (u & 0x7Fu)) << (8 * (c & 3));
+      cw |= uint32_t(code) << (8 * (c & 3) + 4 * (c >> 2));
+    }
+    *reinterpret_cast<uint32_t*>(a.sm + row * kD + 4 * q) = smw[0];
+    *reinterpret_cast<uint32_t*>(a.sm + row * kD + 64 + 4 * q) = smw[1];
+    *reinterpret_cast<uint32_t*>(a.code + row * (kD / 2) + 4 * q) = cw;
+    escrow |= (esc ? 1u : 0u) << i;
+  }
+  if (th == 0) {
+    *reinterpret_cast<uint32_t*>(a.base + page * kD + 4 * q) = bw[0];
+    *reinterpret_cast<uint32_t*>(a.base + page * kD + 64 + 4 * q) = bw[1];
+  }
+  // rowmask: token 8th+i escapes if any of its 16 lanes saw an escape
+  uint32_t rm = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t bal = __ballot_sync(0xFFFFFFFFu, (escrow >> i) & 1u);
+    rm |= ((bal & 0xFFFFu) ? 1u : 0u) << i;
+    rm |= ((bal >> 16) ? 1u : 0u) << (8 + i);
+  }
+  if (lane == 0) a.rowmask[page] = static_cast<int32_t>(rm);
+}
+
+// One CTA: exclusive prefix of the launch's per-page raw-row counts, starting
+// at the pool counter, in tiles of 4 page-heads per thread.
+__global__ void __launch_bounds__(kScanThreads) raw_offsets_kernel(const __grid_constant__ EncArgs a) {
+  __shared__ int s_warp[kScanThreads / 32];
+  __shared__ int s_total;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int carry = *a.cnt;
+  for (int tile = 0; tile < a.n_ph; tile += 4 * kScanThreads) {
+    int cnt[4];
+    int64_t idx[4];
+    int local = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int ph = tile + 4 * threadIdx.x + j;
+      cnt[j] = 0;
+      idx[j] = -1;
+      if (ph < a.n_ph) {
+        int bi, pg, hk;
+        idx[j] = page_index(a, ph, bi, pg, hk);
+        cnt[j] = __popc(static_cast<uint32_t>(a.rowmask[idx[j]]) & 0xFFFFu);
       }
+      local += cnt[j];
+    }
+    int incl = local;  // inclusive scan within the warp
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int y = __shfl_up_sync(0xFFFFFFFFu, incl, d);
+      if (lane >= d) incl += y;
+    }
+    if (lane == 31) s_warp[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+      int w = s_warp[lane];
+      int wi = w;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int y = __shfl_up_sync(0xFFFFFFFFu, wi, d);
+        if (lane >= d) wi += y;
+      }
+      s_warp[lane] = wi - w;  // exclusive per warp
+      if (lane == 31) s_total = wi;
+    }
+    __syncthreads();
+    int off = carry + s_warp[warp] + incl - local;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (idx[j] >= 0) a.rowoff[idx[j]] = off;
+      off += cnt[j];
+    }
+    carry += s_total;
+    __syncthreads();  // s_warp / s_total are rewritten by the next tile
+  }
+  if (threadIdx.x == 0) *a.cnt = carry;  // may exceed raw_cap: the caller grows the pool
+}
+
+// One warp per page-head with raw rows: copies each escaped row from the
+// source into pool row rowoff + rank; rows at or past raw_cap are skipped.
+template <bool VEC>
+__global__ void __launch_bounds__(kEncWarps * 32) raw_copy_kernel(const __grid_constant__ EncArgs a) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ph = blockIdx.x * kEncWarps + warp;
+  if (ph >= a.n_ph) return;
+  int bi, pg, hk;
+  const int64_t page = page_index(a, ph, bi, pg, hk);
+  uint32_t rm = static_cast<uint32_t>(a.rowmask[page]) & 0xFFFFu;
+  if (rm == 0u) return;
+  const int64_t ro = a.rowoff[page];
+  int rank = 0;
+  while (rm != 0u) {
+    const int tok = __ffs(rm) - 1;
+    rm &= rm - 1u;
+    const int64_t ridx = ro + rank++;
+    if (ridx < 0 || ridx >= a.raw_cap) continue;
+    const uint16_t* s = a.src + bi * a.s_b + pg * a.s_pg + static_cast<int64_t>(tok) * a.s_p + hk * a.s_h;
+    uint16_t* d = a.raw + ridx * kD;
+    if constexpr (VEC) {
+      reinterpret_cast<uint2*>(d)[lane] = reinterpret_cast<const uint2*>(s)[lane];
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) d[4 * lane + j] = s[4 * lane + j];
     }
   }
 }
@@ -287,15 +296,17 @@ using namespace exk;
 
 extern "C" int exk_encode_pages(const uint16_t* src, int64_t s_b, int64_t s_pg, int64_t s_p, int64_t s_h,
                                 uint8_t* sm, uint8_t* code, uint8_t* base, int32_t* rowmask, int32_t* rowoff,
-                                uint16_t* raw, int64_t raw_cap, int32_t* cnt, int32_t* chain, int b0, int pg0,
-                                int nb, int npg, int H, int TS, int32_t* status, int device, void* stream) {
+                                uint16_t* raw, int64_t raw_cap, int32_t* cnt, int b0, int pg0, int nb, int npg, int H,
+                                int TS, int32_t* status, int device, void* stream) {
+  (void)status;  // the encoder has no waits and no metadata-driven reads to report
   if (src == nullptr || sm == nullptr || code == nullptr || base == nullptr || rowmask == nullptr ||
-      rowoff == nullptr || raw == nullptr || cnt == nullptr || chain == nullptr || status == nullptr)
+      rowoff == nullptr || raw == nullptr || cnt == nullptr)
     return EXK_EARG;
   if (nb <= 0 || npg <= 0 || H <= 0 || TS <= 0 || TS % kP != 0 || b0 < 0 || pg0 < 0 || raw_cap < 0) return EXK_EARG;
   if ((pg0 + npg) * kP > TS) return EXK_EARG;
   const int64_t n_ph = static_cast<int64_t>(nb) * npg * H;
   if (n_ph > (int64_t{1} << 30)) return EXK_EARG;
+  if ((reinterpret_cast<uintptr_t>(raw) & 7u) != 0) return EXK_EALIGN;
   int r = use_device(device, nullptr);
   if (r != 0) return r;
   EncArgs a;
@@ -312,8 +323,6 @@ extern "C" int exk_encode_pages(const uint16_t* src, int64_t s_b, int64_t s_pg, 
   a.raw = raw;
   a.raw_cap = raw_cap;
   a.cnt = cnt;
-  a.chain = chain;
-  a.status = status;
   a.b0 = b0;
   a.pg0 = pg0;
   a.nb = nb;
@@ -322,14 +331,22 @@ extern "C" int exk_encode_pages(const uint16_t* src, int64_t s_b, int64_t s_pg, 
   a.TS = TS;
   a.NP = TS / kP;
   a.n_ph = static_cast<int>(n_ph);
-  a.n_cta = static_cast<int>((n_ph + kEncWarps - 1) / kEncWarps);
+  const int blocks = static_cast<int>((n_ph + kEncWarps - 1) / kEncWarps);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
   // 8-byte vector loads need every (sequence, page, token, head) start 8-byte aligned
   const bool vec = (reinterpret_cast<uintptr_t>(src) & 7u) == 0 && (s_b % 4) == 0 && (s_pg % 4) == 0 &&
                    (s_p % 4) == 0 && (s_h % 4) == 0;
   if (vec)
-    encode_kernel<true><<<a.n_cta, kEncWarps * 32, 0, static_cast<cudaStream_t>(stream)>>>(a);
+    encode_kernel<true><<<blocks, kEncWarps * 32, 0, st>>>(a);
   else
-    encode_kernel<false><<<a.n_cta, kEncWarps * 32, 0, static_cast<cudaStream_t>(stream)>>>(a);
+    encode_kernel<false><<<blocks, kEncWarps * 32, 0, st>>>(a);
+  if ((r = launch_status()) != 0) return r;
+  raw_offsets_kernel<<<1, kScanThreads, 0, st>>>(a);
+  if ((r = launch_status()) != 0) return r;
+  if (vec)
+    raw_copy_kernel<true><<<blocks, kEncWarps * 32, 0, st>>>(a);
+  else
+    raw_copy_kernel<false><<<blocks, kEncWarps * 32, 0, st>>>(a);
   return launch_status();
 }
 

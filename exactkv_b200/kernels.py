@@ -76,7 +76,6 @@ def _device_index(device):
 # ----------------------------------------------------------------------------- status word and scratch
 
 _STATUS = {}   # device index -> int32[1] status word written by the kernels
-_CHAIN = {}    # (device, stream) -> int32[2] encoder chain state for callers without their own
 
 
 def status_tensor(device):
@@ -97,14 +96,6 @@ def check_status(device=None, reset=True):
             t.zero_()
         raise RuntimeError(f"exactkv_b200 device status {code}: {lib.exk_status_string(code).decode()}")
     return 0
-
-
-def _chain_tensor(device, stream):
-    key = (_device_index(device), stream)
-    t = _CHAIN.get(key)
-    if t is None:
-        t = _CHAIN[key] = torch.zeros(2, dtype=torch.int32, device=device)
-    return t
 
 
 # ----------------------------------------------------------------------------- split workspaces
@@ -226,19 +217,15 @@ def decode_to_bf16(c, T):
 def encode_pages(src, strides, buf, b0, pg0, nb, npg):
     """Encode nb sequences x npg pages. src points at sequence b0's first page to
     encode; strides = (seq, page, token, head) in elements. buf: dict with sm, code,
-    base, rowmask, rowoff, raw, cnt, cap, TS, H, D (and optionally `chain`, the
-    encoder's 2-word scratch; a per-stream one is used otherwise)."""
+    base, rowmask, rowoff, raw, cnt, cap, TS, H, D."""
     if buf["D"] != D or src.dtype != torch.bfloat16 or src.stride(-1) != 1:
         raise ValueError("src must be bf16 with contiguous channels; D = 128 only")
     dev = src.device
     stream = torch.cuda.current_stream(dev).cuda_stream
-    chain = buf.get("chain")
-    if chain is None:
-        chain = _chain_tensor(dev, stream)
     s_b, s_pg, s_p, s_h = (int(s) for s in strides)
     rc = lib.exk_encode_pages(src.data_ptr(), s_b, s_pg, s_p, s_h, buf["sm"].data_ptr(), buf["code"].data_ptr(),
                               buf["base"].data_ptr(), buf["rowmask"].data_ptr(), buf["rowoff"].data_ptr(),
-                              buf["raw"].data_ptr(), int(buf["cap"]), buf["cnt"].data_ptr(), chain.data_ptr(),
+                              buf["raw"].data_ptr(), int(buf["cap"]), buf["cnt"].data_ptr(),
                               b0, pg0, nb, npg, buf["H"], buf["TS"], status_tensor(dev.index).data_ptr(),
                               dev.index, stream)
     check(rc, "exk_encode_pages")

@@ -5,8 +5,8 @@
  * exactkv/kernels.py of the reference. Every entry point takes plain device
  * pointers, element counts and strides, the CUDA device index and a
  * cudaStream_t passed as `void *`. Nothing here allocates device memory: the
- * caller owns every buffer, including the split-K workspace and the 2-word
- * encoder chain state. Work is enqueued on `stream` and nothing synchronises.
+ * caller owns every buffer, including the split-K workspace. Work is enqueued
+ * on `stream` and nothing synchronises.
  *
  * Return value: 0 on success, a positive cudaError_t from the launch, or a
  * negative EXK_E* argument error (exk_error_string() describes every code).
@@ -50,7 +50,7 @@ extern "C" {
 #define EXK_S_FULL_TIMEOUT   1  /* a consumer waited > 2 s for a staged page */
 #define EXK_S_EMPTY_TIMEOUT  2  /* the TMA producer waited > 2 s for a free slot */
 #define EXK_S_RAW_INDEX      3  /* rowoff/rowmask pointed past the raw pool */
-#define EXK_S_CHAIN_TIMEOUT  4  /* encoder CTA waited > 2 s for its predecessor */
+#define EXK_S_CHAIN_TIMEOUT  4  /* (unused: the encoder no longer waits) */
 #define EXK_S_DRAIN_TIMEOUT  5  /* in-flight TMA copies did not land within 2 s */
 
 /* One compressed cache (keys or values of one layer): the six buffers of the
@@ -113,14 +113,13 @@ int exk_attn_merge(const exk_partials *ws, int rows, uint16_t *out, int device, 
  * strides s_b, s_pg, s_p, s_h for sequence, page, token, head; channels
  * contiguous) into sequences b0.. and pages pg0.. of the buffers. Raw rows get
  * pool slots cnt, cnt+1, ... in (sequence, page, head) order — the order of
- * the reference's encode_reference — through a chained scan over CTAs;
- * `cnt` advances even past raw_cap, but slots at or past raw_cap are not
- * written (the caller grows the pool and encodes again). `chain` is 2 int32
- * of zero-initialised scratch, private to the stream; the kernel leaves it
- * zero. Replaces _encode_pages_kernel/encode_pages (exactkv/kernels.py:233-268, 340-346). */
+ * the reference's encode_reference; `cnt` advances even past raw_cap, but
+ * slots at or past raw_cap are not written (the caller grows the pool and
+ * encodes again). Three launches on `stream` (encode, slot scan, raw copy).
+ * Replaces _encode_pages_kernel/encode_pages (exactkv/kernels.py:233-268, 340-346). */
 int exk_encode_pages(const uint16_t *src, int64_t s_b, int64_t s_pg, int64_t s_p, int64_t s_h,
                      uint8_t *sm, uint8_t *code, uint8_t *base, int32_t *rowmask, int32_t *rowoff,
-                     uint16_t *raw, int64_t raw_cap, int32_t *cnt, int32_t *chain,
+                     uint16_t *raw, int64_t raw_cap, int32_t *cnt,
                      int b0, int pg0, int nb, int npg, int H, int TS,
                      int32_t *status, int device, void *stream);
 
