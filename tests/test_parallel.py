@@ -1,0 +1,179 @@
+"""KV-sequence split over ranks (exactkv_b200.parallel).
+
+CPU (gloo, world size 2 and 3): each rank computes its splits' partials with the
+oracle, the packed partials go through the real all-gather and assemble code,
+and the merge of the gathered partials must equal the single-process oracle
+bit for bit (partials depend only on their split's tokens).
+GPU: ranks emulated one after another on one GPU (every rank's cache holds only
+its own pages) must be bit-identical to one kernel run over the whole cache
+with the same plan; with two or more GPUs, the same through NCCL.
+"""
+import os
+import socket
+import tempfile
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from exactkv_b200 import parallel
+from exactkv_b200.parallel import KVSplitPlan, PACK
+from oracle import attention as oatt
+from oracle.bf16 import f32_to_bits
+from oracle.synth import synth_kv, synth_q
+
+D = 128
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_plan_partition_covers_every_split_once():
+    for (ns, sl, T, world) in [(9, 464, 4096, 2), (9, 464, 4096, 4), (3, 48, 130, 8), (128, 1024, 131072, 8),
+                               (5, 16, 70, 3)]:
+        plan = KVSplitPlan(1, 8, T, world, ns, sl)
+        assert plan.bounds[0] == 0 and plan.bounds[-1] == ns
+        assert all(a <= b for a, b in zip(plan.bounds, plan.bounds[1:]))
+        toks = [plan.tokens(r) for r in range(world)]
+        assert toks[0][0] == 0 and toks[-1][1] == T
+        assert all(toks[r][1] == toks[r + 1][0] for r in range(world - 1))
+        assert all(t0 % 16 == 0 for t0, _ in toks)
+    with pytest.raises(ValueError):
+        KVSplitPlan(1, 8, 4096, 2, 4, 464)     # splits do not cover T
+
+
+def _oracle_packed(qb, kb, vb, plan, rank):
+    """Packed partials of one rank, computed by the oracle over the rank's tokens only."""
+    t0, t1 = plan.tokens(rank)
+    B, Hq, _ = qb.shape
+    packed = torch.zeros(B * Hq, plan.max_local, PACK, dtype=torch.float32)
+    if t1 > t0:
+        n = -(-(t1 - t0) // plan.split_len)
+        o, m, l = oatt.split_partials(qb, kb[:, t0:t1], vb[:, t0:t1], t1 - t0, splits=(n, plan.split_len))
+        packed[:, :n, :D] = torch.from_numpy(o.reshape(B * Hq, n, D))
+        packed[:, :n, D] = torch.from_numpy(m.reshape(B * Hq, n))
+        packed[:, :n, D + 1] = torch.from_numpy(l.reshape(B * Hq, n))
+    return packed
+
+
+def _gloo_rank(rank, world, port, args, outdir):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=__import__("datetime").timedelta(seconds=60))
+    try:
+        B, T, Hq, Hkv, ns, sl = args
+        qb, kb, vb = synth_q(11, B, Hq), synth_kv(12, B, T, Hkv), synth_kv(13, B, T, Hkv, key=False)
+        plan = KVSplitPlan(B, Hkv, T, world, ns, sl)
+        gathered = parallel.all_gather_packed(_oracle_packed(qb, kb, vb, plan, rank))
+        o, m, l = parallel.assemble(gathered, plan)
+        out = oatt.merge(o.numpy(), m.numpy(), l.numpy())
+        np.save(os.path.join(outdir, f"out{rank}.npy"), f32_to_bits(out).reshape(B, Hq, D))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,B,T,Hq,Hkv,ns,sl", [(2, 2, 1000, 8, 2, 5, 208), (3, 1, 700, 4, 1, 7, 112)])
+def test_kv_split_gloo_bit_identical(world, B, T, Hq, Hkv, ns, sl):
+    args = (B, T, Hq, Hkv, ns, sl)
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_gloo_rank, args=(world, _free_port(), args, d), nprocs=world, join=True,
+                           start_method="spawn")
+        outs = [np.load(os.path.join(d, f"out{r}.npy")) for r in range(world)]
+    qb, kb, vb = synth_q(11, B, Hq), synth_kv(12, B, T, Hkv), synth_kv(13, B, T, Hkv, key=False)
+    o, m, l = oatt.split_partials(qb, kb, vb, T, splits=(ns, sl))
+    ref = f32_to_bits(oatt.merge(o.reshape(B * Hq, ns, D), m.reshape(B * Hq, ns),
+                                 l.reshape(B * Hq, ns))).reshape(B, Hq, D)
+    for out in outs:
+        assert np.array_equal(out, ref)
+
+
+# ------------------------------------------------------------------ GPU
+
+def _rank_caches(k, v, plan, rank):
+    import exactkv_b200 as ekv
+    t0, t1 = plan.tokens(rank)
+    caches = []
+    for x in (k, v):
+        B, _, H, _ = x.shape
+        TS = max(16, -(-(t1 - t0) // 16) * 16)
+        c = ekv.CompressedKV(B, TS, H, D, reserve=1.0)
+        for b in range(B):
+            if t1 > t0:
+                c.prefill_slot(b, x[b:b + 1, t0:t1].contiguous())
+        caches.append(c)
+    return caches
+
+
+def _full_run(q, k, v, T, ns, sl):
+    import exactkv_b200 as ekv
+    from exactkv_b200 import kernels
+    B, _, H, _ = k.shape
+    TS = -(-T // 16) * 16
+    kc, vc = ekv.CompressedKV(B, TS, H, D, reserve=1.0), ekv.CompressedKV(B, TS, H, D, reserve=1.0)
+    for b in range(B):
+        kc.prefill_slot(b, k[b:b + 1, :T].contiguous())
+        vc.prefill_slot(b, v[b:b + 1, :T].contiguous())
+    Hq = q.shape[1]
+    o = torch.empty(B * Hq, ns, D, device="cuda")
+    m = torch.empty(B * Hq, ns, device="cuda")
+    l = torch.empty(B * Hq, ns, device="cuda")
+    ws = (o, m, l, kernels.Partials(o.data_ptr(), m.data_ptr(), l.data_ptr(), ns, sl))
+    kernels.attention_split(q, kc, vc, T, ws, 0, ns)
+    return parallel.merge(o, m, l, torch.empty_like(q))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("world,B,T,Hq,Hkv", [(2, 1, 8192, 32, 8), (4, 2, 3000, 28, 4), (8, 1, 131072, 32, 8)])
+def test_kv_split_emulated_ranks_bit_identical(world, B, T, Hq, Hkv):
+    from exactkv_b200 import kernels, synthetic
+    k = synthetic.make_kv(B, T, Hkv, seed=21, device="cuda")
+    v = synthetic.make_kv(B, T, Hkv, seed=22, key=False, device="cuda")
+    q = synthetic.make_q(B, Hq, seed=23, device="cuda")
+    plan = KVSplitPlan.make(B, Hkv, T, world)
+    packed = []
+    for r in range(world):
+        kc, vc = _rank_caches(k, v, plan, r)
+        packed.append(parallel.local_partials(q, kc, vc, plan, r))
+    o, m, l = parallel.assemble(packed, plan)
+    out = parallel.merge(o, m, l, torch.empty_like(q))
+    ref = _full_run(q, k, v, T, plan.ns, plan.split_len)
+    kernels.check_status()
+    assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
+
+
+def _nccl_rank(rank, world, port, outdir):
+    import torch.distributed as dist
+    from exactkv_b200 import kernels, synthetic
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                            timeout=__import__("datetime").timedelta(seconds=60))
+    try:
+        B, T, Hq, Hkv = 1, 16384, 32, 8
+        k = synthetic.make_kv(B, T, Hkv, seed=31, device="cuda")
+        v = synthetic.make_kv(B, T, Hkv, seed=32, key=False, device="cuda")
+        q = synthetic.make_q(B, Hq, seed=33, device="cuda")
+        plan = KVSplitPlan.make(B, Hkv, T, world)
+        kc, vc = _rank_caches(k, v, plan, rank)
+        out = parallel.attention_kv_split(q, kc, vc, plan, rank)
+        ref = _full_run(q, k, v, T, plan.ns, plan.split_len)
+        kernels.check_status()
+        ok = torch.equal(out.view(torch.int16), ref.view(torch.int16))
+        open(os.path.join(outdir, f"ok{rank}"), "w").write("1" if ok else "0")
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_kv_split_nccl_bit_identical():
+    world = min(torch.cuda.device_count(), 8)
+    if world < 2:
+        pytest.skip("needs two or more GPUs")
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_nccl_rank, args=(world, _free_port(), d), nprocs=world, join=True, start_method="spawn")
+        assert all(open(os.path.join(d, f"ok{r}")).read() == "1" for r in range(world))
