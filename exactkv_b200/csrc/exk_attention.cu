@@ -76,12 +76,13 @@ struct Cfg {
   static constexpr int kHeads = 8 * NT;                      // query heads per warp (padded)
   static constexpr int kMergeBytes = kWph > 1 ? HG * kHeads * kAccPitch * 4 : 0;
   static constexpr int kMLBytes = 2 * NWC * kHeads * 4;
-  static constexpr int kBudget = 224 * 1024 - kMergeBytes - kMLBytes - 1024;
+  static constexpr int kMetaSlot = COMP ? NWC * 16 : 0;       // per stage: (rowmask, rowoff) x (K, V) per tile
+  static constexpr int kBudget = 224 * 1024 - kMergeBytes - kMLBytes - 4 * kMetaSlot - 1024;
   static constexpr int kStages = (kBudget / kStageBytes) > 4 ? 4 : (kBudget / kStageBytes);
   static_assert(kStages >= 2, "shared memory too small for two stages");
   static constexpr int kRingBytes = kStages * kStageBytes;
   static constexpr int kBarBytes = 2 * kStages * 8 + 16;
-  static constexpr int kBytes = kRingBytes + kMergeBytes + kMLBytes + kBarBytes + 1024;  // + alignment slack
+  static constexpr int kBytes = kRingBytes + kMergeBytes + kMLBytes + kStages * kMetaSlot + kBarBytes + 1024;
   static constexpr uint32_t kTxBytes = static_cast<uint32_t>(kStageBytes);
 };
 
@@ -435,22 +436,6 @@ __device__ __forceinline__ void load_q(const AttnArgs& a, int b, int hk, int g, 
   }
 }
 
-template <bool COMP>
-__device__ __forceinline__ PageMeta load_meta(const AttnArgs& a, int b, int hk, int pg) {
-  PageMeta pm;
-  if constexpr (COMP) {
-    const int64_t idx = (static_cast<int64_t>(b) * a.NP + pg) * a.Hkv + hk;
-    pm.rm[0] = static_cast<uint32_t>(__ldg(a.rowmask[0] + idx)) & 0xFFFFu;
-    pm.rm[1] = static_cast<uint32_t>(__ldg(a.rowmask[1] + idx)) & 0xFFFFu;
-    pm.ro[0] = __ldg(a.rowoff[0] + idx);
-    pm.ro[1] = __ldg(a.rowoff[1] + idx);
-  } else {
-    pm.rm[0] = pm.rm[1] = 0u;
-    pm.ro[0] = pm.ro[1] = 0;
-  }
-  return pm;
-}
-
 // ------------------------------------------------------------------ kernel
 
 template <bool COMP, int NT, int NWC, int HG>
@@ -468,7 +453,9 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
   float* macc = reinterpret_cast<float*>(ring + C::kRingBytes);
   float* mbuf = reinterpret_cast<float*>(ring + C::kRingBytes + C::kMergeBytes);
   float* lbuf = mbuf + NWC * H8;
-  uint64_t* full = reinterpret_cast<uint64_t*>(lbuf + NWC * H8);
+  // page metadata of every stage, written by the producer: [slot][tile] = (rowmask K, rowoff K, rowmask V, rowoff V)
+  int4* meta = reinterpret_cast<int4*>(lbuf + NWC * H8);
+  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(meta) + S * C::kMetaSlot);
   uint64_t* empty = full + S;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + S);
 
@@ -510,8 +497,11 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
         const int row = it.b * a.TS + pg * kP;
         const int h0 = it.hg * HG;
         uint8_t* st = ring + slot * C::kStageBytes;
-        mbar_arrive_expect_tx(&full[slot], C::kTxBytes);
         if constexpr (COMP) {
+          // The tiles' page metadata goes beside the stage: the producer's loads
+          // overlap the stage's copies, and the consumers read it from shared
+          // memory after the same barrier (the arrive below releases the stores).
+          mbar_expect_tx(&full[slot], C::kTxBytes);
           const int prow = it.b * a.NP + pg;
           tma_load_3d(st, &tm.m[0], 0, row, h0, &full[slot]);
           tma_load_3d(st + NWC * 2048, &tm.m[3], 0, row, h0, &full[slot]);
@@ -519,7 +509,22 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
           tma_load_3d(st + NWC * 5120, &tm.m[4], 0, row, h0, &full[slot]);
           tma_load_3d(st + NWC * 6144, &tm.m[2], 0, prow, h0, &full[slot]);
           tma_load_3d(st + NWC * 6272, &tm.m[5], 0, prow, h0, &full[slot]);
+          int4 md[NWC];
+#pragma unroll
+          for (int u = 0; u < NWC; ++u) {  // tile u = (head u / WPH, page phase u % WPH)
+            const int page = pg + u % WPH;
+            md[u] = make_int4(0, 0, 0, 0);
+            if (page < it.page0 + it.npages) {
+              const int64_t idx = (static_cast<int64_t>(it.b) * a.NP + page) * a.Hkv + h0 + u / WPH;
+              md[u] = make_int4(__ldg(a.rowmask[0] + idx), __ldg(a.rowoff[0] + idx), __ldg(a.rowmask[1] + idx),
+                                __ldg(a.rowoff[1] + idx));
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < NWC; ++u) meta[slot * NWC + u] = md[u];
+          mbar_arrive(&full[slot]);
         } else {
+          mbar_arrive_expect_tx(&full[slot], C::kTxBytes);
           tma_load_3d(st, &tm.m[0], 0, row, h0, &full[slot]);
           tma_load_3d(st + NWC * 2048, &tm.m[0], 64, row, h0, &full[slot]);
           tma_load_3d(st + 2 * NWC * 2048, &tm.m[1], 0, row, h0, &full[slot]);
@@ -557,12 +562,8 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
 #pragma unroll
       for (int mm = 0; mm < 8; ++mm) st.acc[nt][mm][0] = st.acc[nt][mm][1] = st.acc[nt][mm][2] = st.acc[nt][mm][3] = 0.f;
     }
-    PageMeta pm_next;
-    if (ph < it.npages) pm_next = load_meta<COMP>(a, it.b, hk, it.page0 + ph);
     for (int s = 0; s < nst; ++s, ++gs) {
       const int p = s * WPH + ph;  // page of the item this warp takes from the stage
-      const PageMeta pm = pm_next;
-      if (p + WPH < it.npages) pm_next = load_meta<COMP>(a, it.b, hk, it.page0 + p + WPH);
       const int slot = gs % S;
       if (!aborted) {
         if (*abort_flag) {
@@ -575,6 +576,17 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
       }
       if (!aborted) {
         if (p < it.npages) {
+          PageMeta pm;
+          if constexpr (COMP) {
+            const int4 v = meta[slot * NWC + warp];  // tile index hl * WPH + ph == warp
+            pm.rm[0] = static_cast<uint32_t>(v.x) & 0xFFFFu;
+            pm.ro[0] = v.y;
+            pm.rm[1] = static_cast<uint32_t>(v.z) & 0xFFFFu;
+            pm.ro[1] = v.w;
+          } else {
+            pm.rm[0] = pm.rm[1] = 0u;
+            pm.ro[0] = pm.ro[1] = 0;
+          }
           const int vr = min(kP, it.tok1 - (it.page0 + p) * kP);
           attend_page<COMP, NT>(tile_ptrs<COMP, NWC, HG>(ring + slot * C::kStageBytes, hl, ph), pm, vr, a, qf, st,
                                 g, t);

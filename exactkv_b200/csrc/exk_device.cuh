@@ -51,15 +51,20 @@ __device__ __forceinline__ uint32_t smem_addr(const void* p) {
 // Outputs: w01 = bf16(value 0) | bf16(value 1) << 16, w23 likewise — the
 // byte order of the inputs decides which values pair up (the attention
 // kernel interleaves two tokens' bytes beforehand to pair along tokens).
+// KILL = false is the decoder for words whose base bytes all have bit 7 clear
+// (no zero group): then adj == bb and the code-0 rule cannot apply.
+template <bool KILL = true>
 __device__ __forceinline__ void dec4(uint32_t smw, uint32_t c, uint32_t adj, uint32_t bb,
                                      uint32_t& w01, uint32_t& w23) {
   uint32_t e = adj + c;
-  // bit 7 of each byte: code >= 1, or not a zero group; PRMT selector 8..B
-  // replicates that bit over its byte, giving a 0x00/0xFF keep mask.
-  uint32_t keep = prmt((c + 0x7F7F7F7Fu) | ~bb, 0u, 0xBA98u);
-  e &= keep;
-  uint32_t hi = (smw & 0x80808080u) | ((e >> 1) & 0x7F7F7F7Fu);  // sign | exponent[7:1]
-  uint32_t lo = (smw & 0x7F7F7F7Fu) | ((e << 7) & 0x80808080u);  // exponent[0] | mantissa
+  if constexpr (KILL) {
+    // bit 7 of each byte: code >= 1, or not a zero group; PRMT selector 8..B
+    // replicates that bit over its byte, giving a 0x00/0xFF keep mask.
+    const uint32_t keep = prmt((c + 0x7F7F7F7Fu) | ~bb, 0u, 0xBA98u);
+    e &= keep;
+  }
+  const uint32_t hi = (smw & 0x80808080u) | ((e >> 1) & 0x7F7F7F7Fu);  // sign | exponent[7:1]
+  const uint32_t lo = (smw & 0x7F7F7F7Fu) | ((e << 7) & 0x80808080u);  // exponent[0] | mantissa
   w01 = prmt(lo, hi, 0x5140u);
   w23 = prmt(lo, hi, 0x7362u);
 }
@@ -79,6 +84,12 @@ __device__ __forceinline__ void fence_mbar_init() {
 
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+               : "memory");
+}
+
+// Adds `bytes` to the transaction count of the current phase without arriving.
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
                : "memory");
 }
 
