@@ -77,12 +77,15 @@ struct Cfg {
   static constexpr int kMergeBytes = kWph > 1 ? HG * kHeads * kAccPitch * 4 : 0;
   static constexpr int kMLBytes = 2 * NWC * kHeads * 4;
   static constexpr int kMetaSlot = COMP ? NWC * 16 : 0;       // per stage: (rowmask, rowoff) x (K, V) per tile
-  static constexpr int kBudget = 224 * 1024 - kMergeBytes - kMLBytes - 4 * kMetaSlot - 1024;
+  static constexpr int kRawRows = COMP ? 16 : 0;              // raw rows staged per stage
+  static constexpr int kRawSlot = kRawRows * kD * 2;
+  static constexpr int kBudget = 224 * 1024 - kMergeBytes - kMLBytes - 4 * (kMetaSlot + kRawSlot) - 1024;
   static constexpr int kStages = (kBudget / kStageBytes) > 4 ? 4 : (kBudget / kStageBytes);
   static_assert(kStages >= 2, "shared memory too small for two stages");
   static constexpr int kRingBytes = kStages * kStageBytes;
   static constexpr int kBarBytes = 2 * kStages * 8 + 16;
-  static constexpr int kBytes = kRingBytes + kMergeBytes + kMLBytes + kStages * kMetaSlot + kBarBytes + 1024;
+  static constexpr int kBytes =
+      kRingBytes + kStages * kRawSlot + kMergeBytes + kMLBytes + kStages * kMetaSlot + kBarBytes + 1024;
   static constexpr uint32_t kTxBytes = static_cast<uint32_t>(kStageBytes);
 };
 
@@ -246,21 +249,29 @@ __device__ __forceinline__ void load_v_bf16(const Slot& s, int g, int t, uint32_
   }
 }
 
-// Pool row of raw token `r` of a page, or -1 (and a status) when the
+// The raw rows of one page-tile: row j (its rank among the page's raw rows)
+// at p + j * 128, for j < lim. p is the stage's shared-memory copy made by
+// the producer, or the global pool when the rows were not staged.
+struct RawRows {
+  const uint16_t* p;
+  int lim;
+};
+
+// Row of raw token `r` of a page, or nullptr (and a status) when the
 // metadata points outside the pool.
-__device__ __forceinline__ int64_t raw_index(uint32_t rm, int32_t ro, int r, int64_t rows, int32_t* status) {
-  const int64_t idx = static_cast<int64_t>(ro) + __popc(rm & ((1u << r) - 1u));
-  if (idx < 0 || idx >= rows) {
+__device__ __forceinline__ const uint4* raw_row(uint32_t rm, const RawRows& src, int r, int32_t* status) {
+  const int j = __popc(rm & ((1u << r) - 1u));
+  if (src.p == nullptr || j >= src.lim) {
     set_status(status, EXK_S_RAW_INDEX);
-    return -1;
+    return nullptr;
   }
-  return idx;
+  return reinterpret_cast<const uint4*>(src.p + static_cast<int64_t>(j) * kD);
 }
 
 // Rows flagged in `fl` are replaced: raw rows (bit set in rm) by their pool
 // row, rows past the valid tokens by zeros (the reference loads them as 0).
-__device__ __forceinline__ void fix_k_rows(uint32_t fl, uint32_t rm, int32_t ro, const uint16_t* raw, int64_t rows,
-                                           int32_t* status, int vr, int g, int t, uint32_t (&kw)[2][16]) {
+__device__ __forceinline__ void fix_k_rows(uint32_t fl, uint32_t rm, const RawRows& src, int32_t* status, int vr,
+                                           int g, int t, uint32_t (&kw)[2][16]) {
 #pragma unroll
   for (int rr = 0; rr < 2; ++rr) {
     const int r = sigma(g) + 8 * rr;
@@ -268,11 +279,10 @@ __device__ __forceinline__ void fix_k_rows(uint32_t fl, uint32_t rm, int32_t ro,
       uint32_t w[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) w[i] = 0u;
-      if (r < vr && raw != nullptr && ((rm >> r) & 1u)) {
-        const int64_t idx = raw_index(rm, ro, r, rows, status);
-        if (idx >= 0) {
-          const uint4* src = reinterpret_cast<const uint4*>(raw + idx * kD);
-          const uint4 a = src[2 * t], b = src[2 * t + 1], c = src[8 + 2 * t], d = src[8 + 2 * t + 1];
+      if (r < vr && ((rm >> r) & 1u)) {
+        const uint4* row = raw_row(rm, src, r, status);
+        if (row != nullptr) {
+          const uint4 a = row[2 * t], b = row[2 * t + 1], c = row[8 + 2 * t], d = row[8 + 2 * t + 1];
           const uint32_t x[16] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w, c.x, c.y, c.z, c.w, d.x, d.y, d.z, d.w};
 #pragma unroll
           for (int i = 0; i < 16; ++i) w[i] = x[i];
@@ -284,22 +294,21 @@ __device__ __forceinline__ void fix_k_rows(uint32_t fl, uint32_t rm, int32_t ro,
   }
 }
 
-__device__ __forceinline__ void raw_v_words(uint32_t fl, uint32_t rm, int32_t ro, const uint16_t* raw, int64_t rows,
-                                            int32_t* status, int vr, int r, int g, uint32_t (&w)[8]) {
+__device__ __forceinline__ void raw_v_words(uint32_t fl, uint32_t rm, const RawRows& src, int32_t* status, int vr,
+                                            int r, int g, uint32_t (&w)[8]) {
 #pragma unroll
   for (int i = 0; i < 8; ++i) w[i] = 0u;
-  if (((fl >> r) & 1u) && r < vr && raw != nullptr && ((rm >> r) & 1u)) {
-    const int64_t idx = raw_index(rm, ro, r, rows, status);
-    if (idx >= 0) {
-      const uint4* src = reinterpret_cast<const uint4*>(raw + idx * kD);
-      const uint4 a = src[g], b = src[8 + g];
+  if (((fl >> r) & 1u) && r < vr && ((rm >> r) & 1u)) {
+    const uint4* row = raw_row(rm, src, r, status);
+    if (row != nullptr) {
+      const uint4 a = row[g], b = row[8 + g];
       w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w; w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
     }
   }
 }
 
-__device__ __forceinline__ void fix_v_rows(uint32_t fl, uint32_t rm, int32_t ro, const uint16_t* raw, int64_t rows,
-                                           int32_t* status, int vr, int g, int t, uint32_t (&vw)[2][8][2]) {
+__device__ __forceinline__ void fix_v_rows(uint32_t fl, uint32_t rm, const RawRows& src, int32_t* status, int vr,
+                                           int g, int t, uint32_t (&vw)[2][8][2]) {
 #pragma unroll
   for (int pp = 0; pp < 2; ++pp) {
     const int ra = sigma(2 * t) + 8 * pp;
@@ -307,8 +316,8 @@ __device__ __forceinline__ void fix_v_rows(uint32_t fl, uint32_t rm, int32_t ro,
     const bool fa = (fl >> ra) & 1u, fb = (fl >> rb) & 1u;
     if (fa || fb) {
       uint32_t wa[8], wb[8];
-      raw_v_words(fl, rm, ro, raw, rows, status, vr, ra, g, wa);
-      raw_v_words(fl, rm, ro, raw, rows, status, vr, rb, g, wb);
+      raw_v_words(fl, rm, src, status, vr, ra, g, wa);
+      raw_v_words(fl, rm, src, status, vr, rb, g, wb);
       const uint32_t mask = (fa ? 0x0000FFFFu : 0u) | (fb ? 0xFFFF0000u : 0u);
 #pragma unroll
       for (int mm = 0; mm < 8; ++mm) {
@@ -331,11 +340,14 @@ struct WarpState {
 };
 
 struct PageMeta {
-  uint32_t rm[2];  // rowmask K, V
-  int32_t ro[2];   // rowoff K, V
+  uint32_t rm[2];   // rowmask K, V
+  RawRows src[2];   // where the page's raw rows of K, V are read
 };
 
-template <bool COMP, int NT>
+// One page of the warp. FIX = false is the body for a full page without raw
+// rows (no fixup code at all, so nothing splits the decode / mma schedule);
+// FIX = true also replaces raw rows and masks rows past the valid tokens.
+template <bool COMP, int NT, bool FIX>
 __device__ __forceinline__ void attend_page(const Slot& s, const PageMeta& pm, int vr, const AttnArgs& a,
                                             const uint32_t (&qf)[NT][16], WarpState<NT>& st, int g, int t) {
   const uint32_t tailmask = vr < kP ? (0xFFFFu & ~((1u << vr) - 1u)) : 0u;
@@ -343,9 +355,9 @@ __device__ __forceinline__ void attend_page(const Slot& s, const PageMeta& pm, i
   // ---- S^T = K . Q^T
   uint32_t kw[2][16];
   if constexpr (COMP) load_k_comp(s, g, t, kw); else load_k_bf16(s, g, t, kw);
-  {
+  if constexpr (FIX) {
     const uint32_t fl = (COMP ? pm.rm[0] : 0u) | tailmask;
-    if (fl != 0u) fix_k_rows(fl, pm.rm[0], pm.ro[0], COMP ? a.raw[0] : nullptr, a.raw_rows[0], a.status, vr, g, t, kw);
+    if (fl != 0u) fix_k_rows(fl, pm.rm[0], pm.src[0], a.status, vr, g, t, kw);
   }
   // two independent accumulation chains (low and high channel halves), summed
   float sc[NT][4];
@@ -367,9 +379,9 @@ __device__ __forceinline__ void attend_page(const Slot& s, const PageMeta& pm, i
   // ---- V fragments (issued before the softmax so the shared loads overlap it)
   uint32_t vw[2][8][2];
   if constexpr (COMP) load_v_comp(s, g, t, vw); else load_v_bf16(s, g, t, vw);
-  {
+  if constexpr (FIX) {
     const uint32_t fl = (COMP ? pm.rm[1] : 0u) | tailmask;
-    if (fl != 0u) fix_v_rows(fl, pm.rm[1], pm.ro[1], COMP ? a.raw[1] : nullptr, a.raw_rows[1], a.status, vr, g, t, vw);
+    if (fl != 0u) fix_v_rows(fl, pm.rm[1], pm.src[1], a.status, vr, g, t, vw);
   }
 
   // ---- online softmax (base 2) over the page's 16 rows
@@ -381,8 +393,10 @@ __device__ __forceinline__ void attend_page(const Slot& s, const PageMeta& pm, i
     float p[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) p[i] = sc[nt][i] * a.qk_scale;
-    if (r0 >= vr) p[0] = p[1] = -INFINITY;
-    if (r1 >= vr) p[2] = p[3] = -INFINITY;
+    if constexpr (FIX) {
+      if (r0 >= vr) p[0] = p[1] = -INFINITY;
+      if (r1 >= vr) p[2] = p[3] = -INFINITY;
+    }
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
       float mx = fmaxf(p[j], p[2 + j]);
@@ -450,8 +464,10 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
   // round trip), so every access below stays a shared-memory access (LDS/STS)
   // rather than a generic one.
   uint8_t* ring = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
-  float* macc = reinterpret_cast<float*>(ring + C::kRingBytes);
-  float* mbuf = reinterpret_cast<float*>(ring + C::kRingBytes + C::kMergeBytes);
+  // raw rows of every stage, copied by the producer: [slot][kRawRows][128] bf16
+  uint16_t* rawbuf = reinterpret_cast<uint16_t*>(ring + C::kRingBytes);
+  float* macc = reinterpret_cast<float*>(ring + C::kRingBytes + S * C::kRawSlot);
+  float* mbuf = reinterpret_cast<float*>(ring + C::kRingBytes + S * C::kRawSlot + C::kMergeBytes);
   float* lbuf = mbuf + NWC * H8;
   // page metadata of every stage, written by the producer: [slot][tile] = (rowmask K, rowoff K, rowmask V, rowoff V)
   int4* meta = reinterpret_cast<int4*>(lbuf + NWC * H8);
@@ -471,36 +487,58 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
   __syncthreads();
 
   if (warp == NWC) {
-    // ------------------------------------------------ TMA producer (one lane)
-    if (lane != 0) return;
-    constexpr int nmaps = COMP ? 6 : 2;
-    for (int i = 0; i < nmaps; ++i) prefetch_tmap(&tm.m[i]);
+    // ------------------------------------------------ producer warp
+    // Per stage: lane 0 issues the tiles' TMA copies; lane u < NWC holds tile
+    // u's page metadata (rowmask K, rowoff K, rowmask V, rowoff V), loaded one
+    // stage ahead; lanes 2u + kv stage tile u's raw rows of cache kv into the
+    // stage's raw area (positions from a warp prefix sum; bulk copies that
+    // complete on the stage's barrier) while it has room, and bits 16-23 of the
+    // rowmask the consumers read give the staged position (0xFF: read the pool).
+    // The metadata goes beside the stage; lane 0's arrive releases it.
+    if (lane == 0) {
+      constexpr int nmaps = COMP ? 6 : 2;
+      for (int i = 0; i < nmaps; ++i) prefetch_tmap(&tm.m[i]);
+    }
+    auto tile_meta = [&](const Item& it_, int s_) {
+      int4 r = make_int4(0, 0, 0, 0);
+      if constexpr (COMP) {
+        const int page = it_.page0 + s_ * WPH + lane % WPH;
+        if (lane < NWC && page < it_.page0 + it_.npages) {
+          const int64_t idx = (static_cast<int64_t>(it_.b) * a.NP + page) * a.Hkv + it_.hg * HG + lane / WPH;
+          r = make_int4(__ldg(a.rowmask[0] + idx), __ldg(a.rowoff[0] + idx), __ldg(a.rowmask[1] + idx),
+                        __ldg(a.rowoff[1] + idx));
+        }
+      }
+      return r;
+    };
+    int item = blockIdx.x, s = 0, nst = 0;
+    Item it{};
+    if (item < a.n_items) {
+      it = decode_item(a, item);
+      nst = (it.npages + WPH - 1) / WPH;
+    }
+    int4 md = item < a.n_items ? tile_meta(it, 0) : make_int4(0, 0, 0, 0);
     uint32_t gs = 0;  // stages issued
-    bool ok = true;
-    for (int item = blockIdx.x; ok && item < a.n_items; item += gridDim.x) {
-      const Item it = decode_item(a, item);
-      const int nst = (it.npages + WPH - 1) / WPH;
-      for (int s = 0; s < nst; ++s, ++gs) {
-        const int slot = gs % S;
-        const uint32_t round = gs / S;
-        if (round > 0 && !mbar_wait(&empty[slot], (round - 1) & 1u)) {
-          set_status(a.status, EXK_S_EMPTY_TIMEOUT);
-          *abort_flag = 1;
-          ok = false;
+    while (item < a.n_items) {
+      const int slot = gs % S;
+      const uint32_t round = gs / S;
+      if (round > 0) {
+        const bool w = mbar_wait(&empty[slot], (round - 1) & 1u);
+        if (!__all_sync(0xFFFFFFFFu, w)) {
+          if (lane == 0) {
+            set_status(a.status, EXK_S_EMPTY_TIMEOUT);
+            *abort_flag = 1;
+          }
           break;
         }
-        if (*abort_flag) {
-          ok = false;
-          break;
-        }
-        const int pg = it.page0 + s * WPH;
-        const int row = it.b * a.TS + pg * kP;
-        const int h0 = it.hg * HG;
-        uint8_t* st = ring + slot * C::kStageBytes;
-        if constexpr (COMP) {
-          // The tiles' page metadata goes beside the stage: the producer's loads
-          // overlap the stage's copies, and the consumers read it from shared
-          // memory after the same barrier (the arrive below releases the stores).
+      }
+      if (__any_sync(0xFFFFFFFFu, *abort_flag != 0)) break;
+      const int pg = it.page0 + s * WPH;
+      const int row = it.b * a.TS + pg * kP;
+      const int h0 = it.hg * HG;
+      uint8_t* st = ring + slot * C::kStageBytes;
+      if constexpr (COMP) {
+        if (lane == 0) {
           mbar_expect_tx(&full[slot], C::kTxBytes);
           const int prow = it.b * a.NP + pg;
           tma_load_3d(st, &tm.m[0], 0, row, h0, &full[slot]);
@@ -509,21 +547,36 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
           tma_load_3d(st + NWC * 5120, &tm.m[4], 0, row, h0, &full[slot]);
           tma_load_3d(st + NWC * 6144, &tm.m[2], 0, prow, h0, &full[slot]);
           tma_load_3d(st + NWC * 6272, &tm.m[5], 0, prow, h0, &full[slot]);
-          int4 md[NWC];
+        }
+        const int tu = lane >> 1, kv = lane & 1;
+        const int x = __shfl_sync(0xFFFFFFFFu, md.x, tu), y = __shfl_sync(0xFFFFFFFFu, md.y, tu);
+        const int z = __shfl_sync(0xFFFFFFFFu, md.z, tu), w = __shfl_sync(0xFFFFFFFFu, md.w, tu);
+        const uint32_t rm = static_cast<uint32_t>(kv ? z : x) & 0xFFFFu;
+        const int ro = kv ? w : y;
+        const int cnt = lane < 2 * NWC ? __popc(rm) : 0;
+        int incl = cnt;  // inclusive prefix sum over the lanes
 #pragma unroll
-          for (int u = 0; u < NWC; ++u) {  // tile u = (head u / WPH, page phase u % WPH)
-            const int page = pg + u % WPH;
-            md[u] = make_int4(0, 0, 0, 0);
-            if (page < it.page0 + it.npages) {
-              const int64_t idx = (static_cast<int64_t>(it.b) * a.NP + page) * a.Hkv + h0 + u / WPH;
-              md[u] = make_int4(__ldg(a.rowmask[0] + idx), __ldg(a.rowoff[0] + idx), __ldg(a.rowmask[1] + idx),
-                                __ldg(a.rowoff[1] + idx));
-            }
-          }
-#pragma unroll
-          for (int u = 0; u < NWC; ++u) meta[slot * NWC + u] = md[u];
-          mbar_arrive(&full[slot]);
-        } else {
+        for (int d = 1; d < 32; d <<= 1) {
+          const int o = __shfl_up_sync(0xFFFFFFFFu, incl, d);
+          if (lane >= d) incl += o;
+        }
+        const int off = incl - cnt;
+        uint32_t tag = 0xFFu;
+        if (cnt > 0 && incl <= C::kRawRows && ro >= 0 && static_cast<int64_t>(ro) + cnt <= a.raw_rows[kv]) {
+          const uint32_t bytes = static_cast<uint32_t>(cnt) * kD * 2;
+          mbar_expect_tx(&full[slot], bytes);
+          bulk_g2s(rawbuf + (slot * C::kRawRows + off) * kD, a.raw[kv] + static_cast<int64_t>(ro) * kD, bytes,
+                   &full[slot]);
+          tag = static_cast<uint32_t>(off);
+        }
+        const int enc = static_cast<int>(rm | (tag << 16));
+        const int ek = __shfl_sync(0xFFFFFFFFu, enc, (2 * lane) & 31);
+        const int ev = __shfl_sync(0xFFFFFFFFu, enc, (2 * lane + 1) & 31);
+        if (lane < NWC) meta[slot * NWC + lane] = make_int4(ek, md.y, ev, md.w);
+        __syncwarp();  // every lane's stores and transaction counts come before the arrive
+        if (lane == 0) mbar_arrive(&full[slot]);
+      } else {
+        if (lane == 0) {
           mbar_arrive_expect_tx(&full[slot], C::kTxBytes);
           tma_load_3d(st, &tm.m[0], 0, row, h0, &full[slot]);
           tma_load_3d(st + NWC * 2048, &tm.m[0], 64, row, h0, &full[slot]);
@@ -531,12 +584,24 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
           tma_load_3d(st + 3 * NWC * 2048, &tm.m[1], 64, row, h0, &full[slot]);
         }
       }
+      ++gs;
+      if (++s == nst) {
+        s = 0;
+        item += gridDim.x;
+        if (item < a.n_items) {
+          it = decode_item(a, item);
+          nst = (it.npages + WPH - 1) / WPH;
+        }
+      }
+      if (item < a.n_items) md = tile_meta(it, s);  // the next stage's metadata, in flight during the wait
     }
-    // Every copy this lane issued lands before the CTA may exit.
-    for (uint32_t i = gs > S ? gs - S : 0; i < gs; ++i) {
-      if (!mbar_wait(&full[i % S], (i / S) & 1u)) {
-        set_status(a.status, EXK_S_DRAIN_TIMEOUT);
-        break;
+    // Every copy this warp issued lands before the CTA may exit.
+    if (lane == 0) {
+      for (uint32_t i = gs > S ? gs - S : 0; i < gs; ++i) {
+        if (!mbar_wait(&full[i % S], (i / S) & 1u)) {
+          set_status(a.status, EXK_S_DRAIN_TIMEOUT);
+          break;
+        }
       }
     }
     return;
@@ -577,19 +642,32 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
       if (!aborted) {
         if (p < it.npages) {
           PageMeta pm;
-          if constexpr (COMP) {
-            const int4 v = meta[slot * NWC + warp];  // tile index hl * WPH + ph == warp
-            pm.rm[0] = static_cast<uint32_t>(v.x) & 0xFFFFu;
-            pm.ro[0] = v.y;
-            pm.rm[1] = static_cast<uint32_t>(v.z) & 0xFFFFu;
-            pm.ro[1] = v.w;
-          } else {
-            pm.rm[0] = pm.rm[1] = 0u;
-            pm.ro[0] = pm.ro[1] = 0;
-          }
+          int4 v = make_int4(0, 0, 0, 0);
+          if constexpr (COMP) v = meta[slot * NWC + warp];  // tile index hl * WPH + ph == warp
+          pm.rm[0] = static_cast<uint32_t>(v.x) & 0xFFFFu;
+          pm.rm[1] = static_cast<uint32_t>(v.z) & 0xFFFFu;
           const int vr = min(kP, it.tok1 - (it.page0 + p) * kP);
-          attend_page<COMP, NT>(tile_ptrs<COMP, NWC, HG>(ring + slot * C::kStageBytes, hl, ph), pm, vr, a, qf, st,
-                                g, t);
+          const Slot tl = tile_ptrs<COMP, NWC, HG>(ring + slot * C::kStageBytes, hl, ph);
+          if ((pm.rm[0] | pm.rm[1]) == 0u && vr == kP) {  // warp-uniform
+            attend_page<COMP, NT, false>(tl, pm, vr, a, qf, st, g, t);
+          } else {
+#pragma unroll
+            for (int kv = 0; kv < 2; ++kv) {
+              const uint32_t tag = (static_cast<uint32_t>(kv ? v.z : v.x) >> 16) & 0xFFu;
+              const int ro = kv ? v.w : v.y;
+              pm.src[kv].p = nullptr;
+              pm.src[kv].lim = 0;
+              if (!COMP) continue;
+              if (tag != 0xFFu) {
+                pm.src[kv].p = rawbuf + (slot * C::kRawRows + static_cast<int>(tag)) * kD;
+                pm.src[kv].lim = __popc(pm.rm[kv]);
+              } else if (ro >= 0 && ro < a.raw_rows[kv]) {
+                pm.src[kv].p = a.raw[kv] + static_cast<int64_t>(ro) * kD;
+                pm.src[kv].lim = a.raw_rows[kv] - ro < kP ? static_cast<int>(a.raw_rows[kv] - ro) : kP;
+              }
+            }
+            attend_page<COMP, NT, true>(tl, pm, vr, a, qf, st, g, t);
+          }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);

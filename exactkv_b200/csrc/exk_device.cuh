@@ -130,6 +130,16 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, int x, 
       : "memory");
 }
 
+// Plain bulk copy of `bytes` (a multiple of 16; both addresses 16-byte
+// aligned) from global to this CTA's shared memory, completing on `bar`.
+// No multicast.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_addr(dst)),
+               "l"(static_cast<uint64_t>(__cvta_generic_to_global(src))), "r"(bytes), "r"(smem_addr(bar))
+               : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }
