@@ -33,6 +33,7 @@
 
 namespace exk {
 
+constexpr int kRawArea = 16;              // raw rows staged per stage (compressed kernel)
 constexpr int kAccPitch = 132;            // floats per head row of the merge buffer (bank padding)
 constexpr uint32_t kSigma = 0x27146350u;  // mma row r (0..7) -> page token sigma(r), nibble r
 
@@ -77,7 +78,7 @@ struct Cfg {
   static constexpr int kMergeBytes = kWph > 1 ? HG * kHeads * kAccPitch * 4 : 0;
   static constexpr int kMLBytes = 2 * NWC * kHeads * 4;
   static constexpr int kMetaSlot = COMP ? NWC * 16 : 0;       // per stage: (rowmask, rowoff) x (K, V) per tile
-  static constexpr int kRawRows = COMP ? 16 : 0;              // raw rows staged per stage
+  static constexpr int kRawRows = COMP ? kRawArea : 0;        // raw rows staged per stage
   static constexpr int kRawSlot = kRawRows * kD * 2;
   static constexpr int kBudget = 224 * 1024 - kMergeBytes - kMLBytes - 4 * (kMetaSlot + kRawSlot) - 1024;
   static constexpr int kStages = (kBudget / kStageBytes) > 4 ? 4 : (kBudget / kStageBytes);
@@ -340,14 +341,78 @@ struct WarpState {
 };
 
 struct PageMeta {
-  uint32_t rm[2];   // rowmask K, V
-  RawRows src[2];   // where the page's raw rows of K, V are read
+  uint32_t rm[2];        // rowmask K, V
+  uint32_t tag[2];       // staged position of the page's first raw row of K, V (0xFF: not staged)
+  const uint16_t* area;  // the stage's raw area
+  RawRows src[2];        // general body: where the page's raw rows of K, V are read
 };
 
-// One page of the warp. FIX = false is the body for a full page without raw
-// rows (no fixup code at all, so nothing splits the decode / mma schedule);
-// FIX = true also replaces raw rows and masks rows past the valid tokens.
-template <bool COMP, int NT, bool FIX>
+// Staged raw rows of a full page (see the producer): the lanes whose fragment
+// rows are raw replace them with shared-memory loads. rm: rowmask; area: the
+// stage's raw area (kRawRows rows); tag: the page's first staged row in it.
+// Positions wrap inside the area, so no address can leave it.
+template <int R>
+__device__ __forceinline__ const uint4* staged_row(const uint16_t* area, uint32_t tag, uint32_t rm, int r) {
+  static_assert((R & (R - 1)) == 0, "the raw area holds a power of two of rows");
+  return reinterpret_cast<const uint4*>(area + ((tag + __popc(rm & ((1u << r) - 1u))) & (R - 1)) * kD);
+}
+
+template <int R>
+__device__ __forceinline__ void patch_k_staged(uint32_t rm, uint32_t tag, const uint16_t* area, int g, int t,
+                                               uint32_t (&kw)[2][16]) {
+#pragma unroll
+  for (int rr = 0; rr < 2; ++rr) {
+    const int r = sigma(g) + 8 * rr;
+    if ((rm >> r) & 1u) {
+      const uint4* row = staged_row<R>(area, tag, rm, r);
+      const uint4 a = row[2 * t], b = row[2 * t + 1], c = row[8 + 2 * t], d = row[8 + 2 * t + 1];
+      const uint32_t x[16] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w, c.x, c.y, c.z, c.w, d.x, d.y, d.z, d.w};
+#pragma unroll
+      for (int i = 0; i < 16; ++i) kw[rr][i] = x[i];
+    }
+  }
+}
+
+template <int R>
+__device__ __forceinline__ void patch_v_staged(uint32_t rm, uint32_t tag, const uint16_t* area, int g, int t,
+                                               uint32_t (&vw)[2][8][2]) {
+#pragma unroll
+  for (int pp = 0; pp < 2; ++pp) {
+    const int ra = sigma(2 * t) + 8 * pp;
+    const int rb = sigma(2 * t + 1) + 8 * pp;
+    const bool fa = (rm >> ra) & 1u, fb = (rm >> rb) & 1u;
+    if (fa || fb) {
+      uint32_t wa[8], wb[8];
+#pragma unroll
+      for (int ab = 0; ab < 2; ++ab) {
+        const int r = ab ? rb : ra;
+        uint32_t* w = ab ? wb : wa;
+        const uint4* row = staged_row<R>(area, tag, rm, r);
+        const bool f = ab ? fb : fa;
+        const uint4 x = f ? row[g] : make_uint4(0, 0, 0, 0), y = f ? row[8 + g] : make_uint4(0, 0, 0, 0);
+        w[0] = x.x; w[1] = x.y; w[2] = x.z; w[3] = x.w; w[4] = y.x; w[5] = y.y; w[6] = y.z; w[7] = y.w;
+      }
+      const uint32_t mask = (fa ? 0x0000FFFFu : 0u) | (fb ? 0xFFFF0000u : 0u);
+#pragma unroll
+      for (int mm = 0; mm < 8; ++mm) {
+        const uint32_t n0 = prmt(wa[mm], wb[mm], 0x5410u);
+        const uint32_t n1 = prmt(wa[mm], wb[mm], 0x7632u);
+        vw[pp][mm][0] = (vw[pp][mm][0] & ~mask) | (n0 & mask);
+        vw[pp][mm][1] = (vw[pp][mm][1] & ~mask) | (n1 & mask);
+      }
+    }
+  }
+}
+
+// Page bodies of the warp. kFast: a full page without raw rows (no fixup code
+// at all, so nothing splits the decode / mma schedule). kStaged: a full page
+// whose raw rows were all staged in shared memory by the producer; the lanes
+// whose rows are raw patch them in with shared-memory loads. kGeneral: raw
+// rows read from wherever the metadata says, rows past the valid tokens
+// masked (a sequence's last partial page, or staging ran out of room).
+enum PageMode { kFast = 0, kStaged = 1, kGeneral = 2 };
+
+template <bool COMP, int NT, int MODE>
 __device__ __forceinline__ void attend_page(const Slot& s, const PageMeta& pm, int vr, const AttnArgs& a,
                                             const uint32_t (&qf)[NT][16], WarpState<NT>& st, int g, int t) {
   const uint32_t tailmask = vr < kP ? (0xFFFFu & ~((1u << vr) - 1u)) : 0u;
@@ -355,9 +420,11 @@ __device__ __forceinline__ void attend_page(const Slot& s, const PageMeta& pm, i
   // ---- S^T = K . Q^T
   uint32_t kw[2][16];
   if constexpr (COMP) load_k_comp(s, g, t, kw); else load_k_bf16(s, g, t, kw);
-  if constexpr (FIX) {
+  if constexpr (MODE == kGeneral) {
     const uint32_t fl = (COMP ? pm.rm[0] : 0u) | tailmask;
     if (fl != 0u) fix_k_rows(fl, pm.rm[0], pm.src[0], a.status, vr, g, t, kw);
+  } else if constexpr (MODE == kStaged && COMP) {
+    patch_k_staged<kRawArea>(pm.rm[0], pm.tag[0], pm.area, g, t, kw);
   }
   // two independent accumulation chains (low and high channel halves), summed
   float sc[NT][4];
@@ -379,9 +446,11 @@ __device__ __forceinline__ void attend_page(const Slot& s, const PageMeta& pm, i
   // ---- V fragments (issued before the softmax so the shared loads overlap it)
   uint32_t vw[2][8][2];
   if constexpr (COMP) load_v_comp(s, g, t, vw); else load_v_bf16(s, g, t, vw);
-  if constexpr (FIX) {
+  if constexpr (MODE == kGeneral) {
     const uint32_t fl = (COMP ? pm.rm[1] : 0u) | tailmask;
     if (fl != 0u) fix_v_rows(fl, pm.rm[1], pm.src[1], a.status, vr, g, t, vw);
+  } else if constexpr (MODE == kStaged && COMP) {
+    patch_v_staged<kRawArea>(pm.rm[1], pm.tag[1], pm.area, g, t, vw);
   }
 
   // ---- online softmax (base 2) over the page's 16 rows
@@ -393,7 +462,7 @@ __device__ __forceinline__ void attend_page(const Slot& s, const PageMeta& pm, i
     float p[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) p[i] = sc[nt][i] * a.qk_scale;
-    if constexpr (FIX) {
+    if constexpr (MODE == kGeneral) {
       if (r0 >= vr) p[0] = p[1] = -INFINITY;
       if (r1 >= vr) p[2] = p[3] = -INFINITY;
     }
@@ -646,27 +715,33 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
           if constexpr (COMP) v = meta[slot * NWC + warp];  // tile index hl * WPH + ph == warp
           pm.rm[0] = static_cast<uint32_t>(v.x) & 0xFFFFu;
           pm.rm[1] = static_cast<uint32_t>(v.z) & 0xFFFFu;
+          pm.tag[0] = (static_cast<uint32_t>(v.x) >> 16) & 0xFFu;
+          pm.tag[1] = (static_cast<uint32_t>(v.z) >> 16) & 0xFFu;
+          pm.area = rawbuf + slot * C::kRawRows * kD;
           const int vr = min(kP, it.tok1 - (it.page0 + p) * kP);
           const Slot tl = tile_ptrs<COMP, NWC, HG>(ring + slot * C::kStageBytes, hl, ph);
-          if ((pm.rm[0] | pm.rm[1]) == 0u && vr == kP) {  // warp-uniform
-            attend_page<COMP, NT, false>(tl, pm, vr, a, qf, st, g, t);
+          // warp-uniform choice of the page body
+          if ((pm.rm[0] | pm.rm[1]) == 0u && vr == kP) {
+            attend_page<COMP, NT, kFast>(tl, pm, vr, a, qf, st, g, t);
+          } else if (COMP && vr == kP && (pm.rm[0] == 0u || pm.tag[0] != 0xFFu) &&
+                     (pm.rm[1] == 0u || pm.tag[1] != 0xFFu)) {
+            attend_page<COMP, NT, kStaged>(tl, pm, vr, a, qf, st, g, t);
           } else {
 #pragma unroll
             for (int kv = 0; kv < 2; ++kv) {
-              const uint32_t tag = (static_cast<uint32_t>(kv ? v.z : v.x) >> 16) & 0xFFu;
               const int ro = kv ? v.w : v.y;
               pm.src[kv].p = nullptr;
               pm.src[kv].lim = 0;
               if (!COMP) continue;
-              if (tag != 0xFFu) {
-                pm.src[kv].p = rawbuf + (slot * C::kRawRows + static_cast<int>(tag)) * kD;
+              if (pm.tag[kv] != 0xFFu) {
+                pm.src[kv].p = pm.area + static_cast<int>(pm.tag[kv]) * kD;
                 pm.src[kv].lim = __popc(pm.rm[kv]);
               } else if (ro >= 0 && ro < a.raw_rows[kv]) {
                 pm.src[kv].p = a.raw[kv] + static_cast<int64_t>(ro) * kD;
                 pm.src[kv].lim = a.raw_rows[kv] - ro < kP ? static_cast<int>(a.raw_rows[kv] - ro) : kP;
               }
             }
-            attend_page<COMP, NT, true>(tl, pm, vr, a, qf, st, g, t);
+            attend_page<COMP, NT, kGeneral>(tl, pm, vr, a, qf, st, g, t);
           }
         }
         __syncwarp();
