@@ -194,6 +194,9 @@ __device__ __forceinline__ void load_k_bf16(const Slot& s, int g, int t, uint32_
   }
 }
 
+// VKILL = false: the page's V base bytes have no zero group (checked by the
+// caller), so the code-0 rule is skipped and the base bytes are used as they are.
+template <bool VKILL>
 __device__ __forceinline__ void load_v_comp(const Slot& s, int g, int t, uint32_t (&vw)[2][8][2]) {
   const uint8_t* sm = s.p[3];
   const uint8_t* cd = s.p[4];
@@ -224,10 +227,12 @@ __device__ __forceinline__ void load_v_comp(const Slot& s, int g, int t, uint32_
                             prmt(ac.y, bc.y, 0x7362u)};
 #pragma unroll
     for (int mm = 0; mm < 4; ++mm)
-      dec4(il[mm], lo_nibbles(jc[mm]), eb[mm] & 0x7F7F7F7Fu, eb[mm], vw[pp][mm][0], vw[pp][mm][1]);
+      dec4<VKILL>(il[mm], lo_nibbles(jc[mm]), VKILL ? eb[mm] & 0x7F7F7F7Fu : eb[mm], eb[mm], vw[pp][mm][0],
+                  vw[pp][mm][1]);
 #pragma unroll
     for (int mm = 4; mm < 8; ++mm)
-      dec4(ih[mm - 4], hi_nibbles(jc[mm - 4]), eb[mm] & 0x7F7F7F7Fu, eb[mm], vw[pp][mm][0], vw[pp][mm][1]);
+      dec4<VKILL>(ih[mm - 4], hi_nibbles(jc[mm - 4]), VKILL ? eb[mm] & 0x7F7F7F7Fu : eb[mm], eb[mm], vw[pp][mm][0],
+                  vw[pp][mm][1]);
   }
 }
 
@@ -407,9 +412,11 @@ __device__ __forceinline__ void patch_v_staged(uint32_t rm, uint32_t tag, const 
 // Page bodies of the warp. kFast: a full page without raw rows (no fixup code
 // at all, so nothing splits the decode / mma schedule). kStaged: a full page
 // whose raw rows were all staged in shared memory by the producer; the lanes
-// whose rows are raw patch them in with shared-memory loads. kGeneral: raw
-// rows read from wherever the metadata says, rows past the valid tokens
-// masked (a sequence's last partial page, or staging ran out of room).
+// whose rows are raw patch them in with shared-memory loads. Both need a V
+// page without zero groups (V decodes without the code-0 rule). kGeneral:
+// everything else — raw rows read from wherever the metadata says, rows past
+// the valid tokens masked (a sequence's last partial page, staging out of
+// room, zero groups in V).
 enum PageMode { kFast = 0, kStaged = 1, kGeneral = 2 };
 
 template <bool COMP, int NT, int MODE>
@@ -445,7 +452,7 @@ __device__ __forceinline__ void attend_page(const Slot& s, const PageMeta& pm, i
 
   // ---- V fragments (issued before the softmax so the shared loads overlap it)
   uint32_t vw[2][8][2];
-  if constexpr (COMP) load_v_comp(s, g, t, vw); else load_v_bf16(s, g, t, vw);
+  if constexpr (COMP) load_v_comp<MODE == kGeneral>(s, g, t, vw); else load_v_bf16(s, g, t, vw);
   if constexpr (MODE == kGeneral) {
     const uint32_t fl = (COMP ? pm.rm[1] : 0u) | tailmask;
     if (fl != 0u) fix_v_rows(fl, pm.rm[1], pm.src[1], a.status, vr, g, t, vw);
@@ -721,9 +728,15 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
           const int vr = min(kP, it.tok1 - (it.page0 + p) * kP);
           const Slot tl = tile_ptrs<COMP, NWC, HG>(ring + slot * C::kStageBytes, hl, ph);
           // warp-uniform choice of the page body
-          if ((pm.rm[0] | pm.rm[1]) == 0u && vr == kP) {
+          bool vzero = false;
+          if constexpr (COMP) {
+            const uint2 bl = *reinterpret_cast<const uint2*>(tl.p[5] + 8 * g);
+            const uint2 bh = *reinterpret_cast<const uint2*>(tl.p[5] + 64 + 8 * g);
+            vzero = __any_sync(0xFFFFFFFFu, ((bl.x | bl.y | bh.x | bh.y) & 0x80808080u) != 0u);
+          }
+          if ((pm.rm[0] | pm.rm[1]) == 0u && vr == kP && !vzero) {
             attend_page<COMP, NT, kFast>(tl, pm, vr, a, qf, st, g, t);
-          } else if (COMP && vr == kP && (pm.rm[0] == 0u || pm.tag[0] != 0xFFu) &&
+          } else if (COMP && vr == kP && !vzero && (pm.rm[0] == 0u || pm.tag[0] != 0xFFu) &&
                      (pm.rm[1] == 0u || pm.tag[1] != 0xFFu)) {
             attend_page<COMP, NT, kStaged>(tl, pm, vr, a, qf, st, g, t);
           } else {

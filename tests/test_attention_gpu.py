@@ -118,6 +118,30 @@ def test_attention_llama_shaped_synthetic():
     kernels.check_status()
 
 
+@pytest.mark.parametrize("nw", [4, 8])
+def test_attention_zero_groups_in_values(nw):
+    """Exact zeros (and a denormal) in V make zero groups in V pages, which the kernels
+    decode with the code-0 rule on a separate page body; some pages also carry
+    raw rows, some end partly filled."""
+    B, T, Hq, Hkv = 2, 1500, 32, 8
+    TS = -(-T // 16) * 16
+    k = synthetic.make_kv(B, TS, Hkv, seed=41, key=True)
+    v = synthetic.make_kv(B, TS, Hkv, seed=42, key=False)
+    g = torch.Generator(device="cuda").manual_seed(43)
+    v = torch.where(torch.rand(v.shape, generator=g, device="cuda") < 2e-3, torch.zeros_like(v), v)
+    v[:, 100:116, 3, 5] = 0.0                       # a whole page-channel of zeros
+    v[1, 517, 6, 77] = torch.tensor(2.0 ** -130).to(torch.bfloat16)   # denormal in a zero group
+    q = synthetic.make_q(B, Hq, seed=44)
+    kc, vc = _compress(k), _compress(v)
+    zg = (vc.base[:, :, :, :] >= 128).any(-1).float().mean().item()
+    assert zg > 0.1, zg                             # a good share of V pages has a zero group
+    o_c = kernels.attention_compressed(q, kc, vc, T, num_warps=nw)
+    o_r = kernels.attention_reference(q, k, v, T, num_warps=nw)
+    assert same_bits(o_c, o_r)
+    _check_close(o_c, q, k, v, T)
+    kernels.check_status()
+
+
 def test_attention_split_subsets_match_full_run():
     """Running the plan's splits in two launches ([0, s) and [s, ns)) writes the same
     partials as one launch — the per-GPU step of a KV-sequence split."""
