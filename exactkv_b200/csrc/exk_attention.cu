@@ -526,6 +526,92 @@ __device__ __forceinline__ void load_q(const AttnArgs& a, int b, int hk, int g, 
   }
 }
 
+// ------------------------------------------------------------------ split merge
+
+// out[row] = sum_s w_s o_s / sum_s w_s l_s with w_s = 2^(m_s - max_s m_s), by
+// one warp (the reference's _reduce_kernel, exactkv/kernels.py:33-43). The
+// split weights come from all (m, l) pairs at once (lane s holds split s, 32
+// splits per round); the o rows are summed in split order with their loads
+// batched 8 at a time.
+__device__ __forceinline__ void merge_row(const float* __restrict__ o, const float* __restrict__ m,
+                                          const float* __restrict__ l, int ns, int64_t row, int lane,
+                                          uint16_t* __restrict__ out) {
+  const float* mr = m + row * ns;
+  const float* lr = l + row * ns;
+  const float4* orow = reinterpret_cast<const float4*>(o + row * ns * kD) + lane;
+  if (ns <= 16) {
+    // every load at once (one round trip), then the same sums in the same order
+    const float mv = lane < ns ? __ldcg(mr + lane) : -INFINITY;
+    const float lv = lane < ns ? __ldcg(lr + lane) : 0.f;
+    float4 v[16];
+#pragma unroll
+    for (int u = 0; u < 16; ++u) v[u] = u < ns ? __ldcg(orow + u * (kD / 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    float M = mv;
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, d));
+    const float w = lane < ns ? ex2(mv - M) : 0.f;
+    float den = lane < ns ? w * lv : 0.f;
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) den += __shfl_xor_sync(0xFFFFFFFFu, den, d);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+      const float wu = __shfl_sync(0xFFFFFFFFu, w, u);
+      if (u < ns) {
+        acc.x += wu * v[u].x;
+        acc.y += wu * v[u].y;
+        acc.z += wu * v[u].z;
+        acc.w += wu * v[u].w;
+      }
+    }
+    uint2 r;
+    r.x = pack_bf16x2(acc.x / den, acc.y / den);
+    r.y = pack_bf16x2(acc.z / den, acc.w / den);
+    reinterpret_cast<uint2*>(out + row * kD)[lane] = r;
+    return;
+  }
+  float M = -INFINITY;
+  for (int s0 = 0; s0 < ns; s0 += 32) M = fmaxf(M, s0 + lane < ns ? __ldcg(mr + s0 + lane) : -INFINITY);
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, d));
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float den = 0.f;
+  for (int s0 = 0; s0 < ns; s0 += 32) {
+    const int n = min(32, ns - s0);
+    const float w = lane < n ? ex2(__ldcg(mr + s0 + lane) - M) : 0.f;
+    float lw = lane < n ? w * __ldcg(lr + s0 + lane) : 0.f;
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) lw += __shfl_xor_sync(0xFFFFFFFFu, lw, d);
+    den += lw;
+    int j = 0;
+    for (; j + 8 <= n; j += 8) {
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = __ldcg(orow + static_cast<int64_t>(s0 + j + u) * (kD / 4));
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float wu = __shfl_sync(0xFFFFFFFFu, w, j + u);
+        acc.x += wu * v[u].x;
+        acc.y += wu * v[u].y;
+        acc.z += wu * v[u].z;
+        acc.w += wu * v[u].w;
+      }
+    }
+    for (; j < n; ++j) {
+      const float4 v = __ldcg(orow + static_cast<int64_t>(s0 + j) * (kD / 4));
+      const float wu = __shfl_sync(0xFFFFFFFFu, w, j);
+      acc.x += wu * v.x;
+      acc.y += wu * v.y;
+      acc.z += wu * v.z;
+      acc.w += wu * v.w;
+    }
+  }
+  uint2 r;
+  r.x = pack_bf16x2(acc.x / den, acc.y / den);
+  r.y = pack_bf16x2(acc.z / den, acc.w / den);
+  reinterpret_cast<uint2*>(out + row * kD)[lane] = r;
+}
+
 // ------------------------------------------------------------------ kernel
 
 template <bool COMP, int NT, int NWC, int HG>
@@ -553,6 +639,8 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
+    // a merge launched as a programmatic dependent may start its (waiting) CTAs now
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     for (int i = 0; i < S; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], NWC);
@@ -871,6 +959,7 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
           }
       }
     }
+
   }
 }
 
@@ -879,28 +968,13 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
 __global__ void __launch_bounds__(128) merge_kernel(const float* __restrict__ o, const float* __restrict__ m,
                                                     const float* __restrict__ l, int ns, int rows,
                                                     uint16_t* __restrict__ out) {
+  // Launched as a programmatic dependent of the split kernel: the CTAs may be
+  // resident early; this waits until the split grid has finished and its
+  // partials are visible (a no-op after an ordinary launch).
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int row = blockIdx.x * 4 + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
   if (row >= rows) return;
-  const float* mr = m + static_cast<int64_t>(row) * ns;
-  const float* lr = l + static_cast<int64_t>(row) * ns;
-  float M = -INFINITY;
-  for (int s = 0; s < ns; ++s) M = fmaxf(M, mr[s]);
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  float den = 0.f;
-  for (int s = 0; s < ns; ++s) {
-    const float w = ex2(mr[s] - M);
-    const float4 v = reinterpret_cast<const float4*>(o + (static_cast<int64_t>(row) * ns + s) * kD)[lane];
-    acc.x += w * v.x;
-    acc.y += w * v.y;
-    acc.z += w * v.z;
-    acc.w += w * v.w;
-    den += w * lr[s];
-  }
-  uint2 r;
-  r.x = pack_bf16x2(acc.x / den, acc.y / den);
-  r.y = pack_bf16x2(acc.z / den, acc.w / den);
-  reinterpret_cast<uint2*>(out + static_cast<int64_t>(row) * kD)[lane] = r;
+  merge_row(o, m, l, ns, row, threadIdx.x & 31, out);
 }
 
 
@@ -1043,10 +1117,11 @@ extern "C" int exk_plan_splits(int B, int Hkv, int T, int num_ctas, int32_t* ns_
   return 0;
 }
 
-extern "C" int exk_attn_split_compressed(const uint16_t* q, const exk_cview* k, const exk_cview* v, int B, int TS,
-                                         int Hkv, int Hq, int T, int s0, int s1, const exk_partials* ws,
-                                         int consumer_warps, float qk_scale, int32_t* status, int device,
-                                         void* stream) {
+namespace {
+
+int split_compressed(const uint16_t* q, const exk_cview* k, const exk_cview* v, int B, int TS, int Hkv, int Hq, int T,
+                     int s0, int s1, const exk_partials* ws, int consumer_warps, float qk_scale, int32_t* status,
+                     int device, void* stream) {
   if (k == nullptr || v == nullptr) return EXK_EARG;
   AttnArgs a;
   int r = common_args(a, q, B, TS, Hkv, Hq, T, s0, s1, ws, consumer_warps, qk_scale, status);
@@ -1080,9 +1155,9 @@ extern "C" int exk_attn_split_compressed(const uint16_t* q, const exk_cview* k, 
   return dispatch_split<true>(a, maps, hg, grid, consumer_warps, device, static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int exk_attn_split_bf16(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int TS, int Hkv,
-                                   int Hq, int T, int s0, int s1, const exk_partials* ws, int consumer_warps,
-                                   float qk_scale, int32_t* status, int device, void* stream) {
+int split_bf16(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int TS, int Hkv, int Hq, int T, int s0,
+               int s1, const exk_partials* ws, int consumer_warps, float qk_scale, int32_t* status, int device,
+               void* stream) {
   if (k == nullptr || v == nullptr) return EXK_EARG;
   AttnArgs a;
   int r = common_args(a, q, B, TS, Hkv, Hq, T, s0, s1, ws, consumer_warps, qk_scale, status);
@@ -1104,11 +1179,64 @@ extern "C" int exk_attn_split_bf16(const uint16_t* q, const uint16_t* k, const u
   return dispatch_split<false>(a, maps, hg, grid, consumer_warps, device, static_cast<cudaStream_t>(stream));
 }
 
+// Merge launch: a programmatic dependent of the preceding kernel on the stream
+// (its CTAs are scheduled early and wait in griddepcontrol.wait).
+int launch_merge(const exk_partials* ws, int rows, uint16_t* out, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((rows + 3) / 4);
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, merge_kernel, static_cast<const float*>(ws->o),
+                                           static_cast<const float*>(ws->m), static_cast<const float*>(ws->l), ws->ns,
+                                           rows, out);
+  return e == cudaSuccess ? 0 : static_cast<int>(e);
+}
+
+}  // namespace
+
+extern "C" int exk_attn_split_compressed(const uint16_t* q, const exk_cview* k, const exk_cview* v, int B, int TS,
+                                         int Hkv, int Hq, int T, int s0, int s1, const exk_partials* ws,
+                                         int consumer_warps, float qk_scale, int32_t* status, int device,
+                                         void* stream) {
+  return split_compressed(q, k, v, B, TS, Hkv, Hq, T, s0, s1, ws, consumer_warps, qk_scale, status, device, stream);
+}
+
+extern "C" int exk_attn_split_bf16(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int TS, int Hkv,
+                                   int Hq, int T, int s0, int s1, const exk_partials* ws, int consumer_warps,
+                                   float qk_scale, int32_t* status, int device, void* stream) {
+  return split_bf16(q, k, v, B, TS, Hkv, Hq, T, s0, s1, ws, consumer_warps, qk_scale, status, device, stream);
+}
+
+extern "C" int exk_attention_compressed(const uint16_t* q, const exk_cview* k, const exk_cview* v, int B, int TS,
+                                        int Hkv, int Hq, int T, const exk_partials* ws, uint16_t* out,
+                                        int consumer_warps, float qk_scale, int32_t* status, int device,
+                                        void* stream) {
+  if (ws == nullptr || out == nullptr) return EXK_EARG;
+  if ((reinterpret_cast<uintptr_t>(out) & 7u) != 0) return EXK_EALIGN;
+  int r = split_compressed(q, k, v, B, TS, Hkv, Hq, T, 0, ws->ns, ws, consumer_warps, qk_scale, status, device,
+                           stream);
+  return r != 0 ? r : launch_merge(ws, B * Hq, out, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int exk_attention_bf16(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int TS, int Hkv,
+                                  int Hq, int T, const exk_partials* ws, uint16_t* out, int consumer_warps,
+                                  float qk_scale, int32_t* status, int device, void* stream) {
+  if (ws == nullptr || out == nullptr) return EXK_EARG;
+  if ((reinterpret_cast<uintptr_t>(out) & 7u) != 0) return EXK_EALIGN;
+  int r = split_bf16(q, k, v, B, TS, Hkv, Hq, T, 0, ws->ns, ws, consumer_warps, qk_scale, status, device, stream);
+  return r != 0 ? r : launch_merge(ws, B * Hq, out, static_cast<cudaStream_t>(stream));
+}
+
 extern "C" int exk_attn_merge(const exk_partials* ws, int rows, uint16_t* out, int device, void* stream) {
   if (ws == nullptr || out == nullptr || rows <= 0 || ws->ns <= 0) return EXK_EARG;
   if (!aligned16(ws->o) || (reinterpret_cast<uintptr_t>(out) & 7u) != 0) return EXK_EALIGN;
   int r = use_device(device, nullptr);
   if (r != 0) return r;
-  merge_kernel<<<(rows + 3) / 4, 128, 0, static_cast<cudaStream_t>(stream)>>>(ws->o, ws->m, ws->l, ws->ns, rows, out);
-  return launch_status();
+  return launch_merge(ws, rows, out, static_cast<cudaStream_t>(stream));
 }

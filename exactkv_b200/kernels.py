@@ -104,6 +104,7 @@ _WS = {}  # (device, stream, rows, ns) -> (o, m, l, Partials); reused by calls o
 
 
 def _workspace(device, stream, rows, ns, split_len):
+    """Split partials o [rows, ns, 128], m, l [rows, ns]."""
     key = (device.index, stream, rows, ns)
     ws = _WS.get(key)
     if ws is None:
@@ -172,12 +173,11 @@ def attention_compressed(q, kc, vc, T, BLOCK_N=64, num_warps=None, num_stages=1)
     stream = torch.cuda.current_stream(q.device).cuda_stream
     ns, sl = plan_splits(B, Hkv, T, dev)
     ws = _workspace(q.device, stream, B * Hq, ns, sl)
-    rc = lib.exk_attn_split_compressed(q.data_ptr(), ctypes.byref(ka), ctypes.byref(va), B, TS, Hkv, Hq, T, 0, ns,
-                                       ctypes.byref(ws[3]), _consumer_warps(num_warps), D ** -0.5 * LOG2E,
-                                       status_tensor(dev).data_ptr(), dev, stream)
-    check(rc, "exk_attn_split_compressed")
     out = torch.empty_like(q)
-    check(lib.exk_attn_merge(ctypes.byref(ws[3]), B * Hq, out.data_ptr(), dev, stream), "exk_attn_merge")
+    rc = lib.exk_attention_compressed(q.data_ptr(), ctypes.byref(ka), ctypes.byref(va), B, TS, Hkv, Hq, T,
+                                      ctypes.byref(ws[3]), out.data_ptr(), _consumer_warps(num_warps),
+                                      D ** -0.5 * LOG2E, status_tensor(dev).data_ptr(), dev, stream)
+    check(rc, "exk_attention_compressed")
     return out
 
 
@@ -192,12 +192,11 @@ def attention_reference(q, k, v, T, BLOCK_N=64, num_warps=None, num_stages=1):
     stream = torch.cuda.current_stream(q.device).cuda_stream
     ns, sl = plan_splits(B, Hkv, T, dev)
     ws = _workspace(q.device, stream, B * Hq, ns, sl)
-    rc = lib.exk_attn_split_bf16(q.data_ptr(), k.data_ptr(), v.data_ptr(), B, TS, Hkv, Hq, T, 0, ns,
-                                 ctypes.byref(ws[3]), _consumer_warps(num_warps), D ** -0.5 * LOG2E,
-                                 status_tensor(dev).data_ptr(), dev, stream)
-    check(rc, "exk_attn_split_bf16")
     out = torch.empty_like(q)
-    check(lib.exk_attn_merge(ctypes.byref(ws[3]), B * Hq, out.data_ptr(), dev, stream), "exk_attn_merge")
+    rc = lib.exk_attention_bf16(q.data_ptr(), k.data_ptr(), v.data_ptr(), B, TS, Hkv, Hq, T, ctypes.byref(ws[3]),
+                                out.data_ptr(), _consumer_warps(num_warps), D ** -0.5 * LOG2E,
+                                status_tensor(dev).data_ptr(), dev, stream)
+    check(rc, "exk_attention_bf16")
     return out
 
 

@@ -109,6 +109,23 @@ int exk_attn_split_bf16(const uint16_t *q, const uint16_t *k, const uint16_t *v,
  * Replaces _reduce_kernel (exactkv/kernels.py:33-43). */
 int exk_attn_merge(const exk_partials *ws, int rows, uint16_t *out, int device, void *stream);
 
+/* One whole decode-attention call: every split of the plan in `ws`, then the
+ * merge into bf16 out [B, Hq, 128] (exk_attn_merge), enqueued together; the
+ * merge is a programmatic dependent launch, so its start overlaps the split
+ * kernel's end. Replaces attention_compressed (exactkv/kernels.py:310-318):
+ * the split kernel plus _reduce (exactkv/kernels.py:295-299). */
+int exk_attention_compressed(const uint16_t *q, const exk_cview *k, const exk_cview *v,
+                             int B, int TS, int Hkv, int Hq, int T, const exk_partials *ws,
+                             uint16_t *out, int consumer_warps, float qk_scale,
+                             int32_t *status, int device, void *stream);
+
+/* The bf16 sibling of exk_attention_compressed (bit-identical on the same values,
+ * plan and consumer_warps). Replaces attention_reference (exactkv/kernels.py:321-328). */
+int exk_attention_bf16(const uint16_t *q, const uint16_t *k, const uint16_t *v,
+                       int B, int TS, int Hkv, int Hq, int T, const exk_partials *ws,
+                       uint16_t *out, int consumer_warps, float qk_scale,
+                       int32_t *status, int device, void *stream);
+
 /* Page encoder: encodes nb sequences x npg pages of `src` (bf16 bits, element
  * strides s_b, s_pg, s_p, s_h for sequence, page, token, head; channels
  * contiguous) into sequences b0.. and pages pg0.. of the buffers. Raw rows get
