@@ -30,6 +30,14 @@ host memory, appends them to the caches (encoding a page every 16 steps,
 with the check_overflow sync), runs decode_attention and copies the output
 back to pinned host memory; the context grows by one token per step.
 
+engine: BASELINE configs[4] decode throughput through exactkv_b200.Engine on a
+random-init Llama-3.1-8B (32 layers, hidden 4096, 32 q / 8 kv heads, FFN 14336,
+vocab 128256, bf16 weights ~ N(0, 0.02)), batch sized to the free HBM minus
+1.6 GiB (and the synthetic context's scratch); every sequence's 4096-token
+context is filled with the synthetic KV through the prefill encoder (the
+decode step's cost does not depend on how the context was produced), then
+greedy steps are timed with CUDA events; tok/s summed over ranks.
+
 --impl reference: the reference algorithm on the host CPU (the numpy oracle:
 codec decode + split-K attention) over all host cores, a bounded sample per
 step (one sequence of the batch); rank 0 only.
@@ -64,6 +72,8 @@ def parse_args():
     ap.add_argument("--context", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-engine", action="store_true")
+    ap.add_argument("--engine-steps", type=int, default=24)
     ap.add_argument("--num-warps", type=int, default=8)
     ap.add_argument("--quick", action="store_true",
                     help="few launches for profiling: no warm loop, L2-flushed pass, e2e or CPU baseline")
@@ -287,6 +297,11 @@ def run_ours(a, rank, world, local):
 
     encoder = None if a.quick else time_encoder(kbf, B, T, Hkv, dev)
 
+    engine = None
+    if not (a.no_engine or a.quick):
+        del kbf, vbf
+        engine = run_engine(a, dev, world)
+
     e2e = None
     if not (a.no_e2e or a.quick):
         e2e = run_e2e(a, kc, vc, B, Hq, Hkv, T, dev, world, raw_rows, ns)
@@ -319,6 +334,7 @@ def run_ours(a, rank, world, local):
         "encoder": encoder,
         "clocks": clocks.summary(),
         "e2e": e2e,
+        "engine": engine,
         "cpu_baseline": cpu,
     }
     if rank == 0:
@@ -386,7 +402,7 @@ def run_e2e(a, kc, vc, B, Hq, Hkv, T0, dev, world, raw_rows0, ns0):
         if kc.T % 16 == 0:
             ekv.check_overflow([kc, vc])
         o = ekv.decode_attention(q, kc, vc)
-        o_h[i].copy_(o)                           # device -> host read of the step's result
+        o_h[i].copy_(o, non_blocking=True)        # device -> host read of the step's result (pinned, on the stream)
         T = kc.T
         npt = -(-T // 16)
         # as algorithmic_bytes(): full-page rows, page metadata, the prefill's raw rows and the
@@ -406,8 +422,75 @@ def run_e2e(a, kc, vc, B, Hq, Hkv, T0, dev, world, raw_rows0, ns0):
     return {"value": round(nbytes_total * world / (ms * 1e-3) / 1e12, 4), "unit": UNIT,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms / K, 4),
             "wall_ms_per_step": round(wall / K * 1e3, 4),
-            "what": "per step: H2D q + new K/V token (pinned), append (+page encode / check_overflow every 16), "
-                    "decode_attention, D2H output; context grows from 4096"}
+            "what": "per step: H2D q + new K/V token (pinned), append (+page encode / check_overflow every 16, "
+                    "which syncs), decode_attention, D2H output into pinned memory on the stream; "
+                    "context grows from 4096"}
+
+
+def run_engine(a, dev, world, context=4096, warm=4):
+    """Engine decode tok/s on a random-init Llama-3.1-8B (see the module docstring)."""
+    import gc
+    import torch
+    import torch.distributed as dist
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    import exactkv_b200 as ekv
+    from exactkv_b200 import synthetic
+
+    gc.collect()
+    torch.cuda.empty_cache()
+    cfg = LlamaConfig(vocab_size=128256, hidden_size=4096, intermediate_size=14336, num_hidden_layers=32,
+                      num_attention_heads=32, num_key_value_heads=8, head_dim=128, rope_theta=5e5,
+                      max_position_embeddings=8192, rms_norm_eps=1e-5, initializer_range=0.02,
+                      tie_word_embeddings=False)
+    torch.manual_seed(1234)
+    with torch.device(dev):
+        model = LlamaForCausalLM._from_config(cfg, dtype=torch.bfloat16).eval()
+    steps = a.engine_steps
+    TM = context + warm + steps + 16
+    per_seq = ekv.Engine(model, 2, TM).kv_bytes() - ekv.Engine(model, 1, TM).kv_bytes()
+    torch.cuda.empty_cache()
+    chunk = 16
+    scratch = 2 * chunk * context * 8 * 128 * 2 * 2           # the synthetic K/V chunk (and its copy)
+    budget = torch.cuda.mem_get_info(dev)[0] - int(1.6 * 2 ** 30) - scratch - (2 << 30)   # 2 GiB for activations
+    B = max(1, min(1024, budget // per_seq))
+    eng = ekv.Engine(model, B, TM)
+    for b0 in range(0, B, chunk):
+        n = min(chunk, B - b0)
+        k = synthetic.make_kv(n, context, 8, seed=900 + b0, theta=5e5, key=True, device=dev)
+        v = synthetic.make_kv(n, context, 8, seed=901 + b0, theta=5e5, key=False, device=dev)
+        for kc, vc in eng.kv:
+            for j in range(n):
+                kc.prefill_slot(b0 + j, k[j:j + 1])
+                vc.prefill_slot(b0 + j, v[j:j + 1])
+        del k, v
+    tok = torch.randint(0, cfg.vocab_size, (B,), device=dev)
+    for _ in range(warm):
+        tok = eng.step(tok).argmax(-1)
+    stream = torch.cuda.current_stream(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        tok = eng.step(tok).argmax(-1)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    res = {"tok_s": round(B * steps * world / (ms * 1e-3), 1), "batch_per_gpu": int(B), "context": context,
+           "steps": steps, "ms_per_step": round(ms / steps, 3), "kv_mib_per_seq": round(per_seq / 2 ** 20, 1),
+           "pool_grows": int(eng.grows), "model": "random-init Llama-3.1-8B (bf16)",
+           "what": "greedy decode steps through exactkv_b200.Engine (HF modules + compressed caches), "
+                   "contexts filled with the synthetic KV"}
+    del eng, model
+    gc.collect()
+    torch.cuda.empty_cache()
+    return res
 
 
 # ----------------------------------------------------------------------------- CPU (oracle) legs

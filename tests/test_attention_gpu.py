@@ -164,3 +164,44 @@ def test_attention_split_subsets_match_full_run():
     kernels.merge_partials(ws_b, B * Hq, out)
     assert same_bits(out, ekv.decode_attention(q, kc, vc))
     kernels.check_status()
+
+
+def test_attention_qwen_1x32k():
+    """Qwen2.5-7B shape (28 q / 4 kv), one sequence of 32,768 tokens,
+    RoPE theta 1e6: compressed == bf16 bit for bit, within tolerance of float64."""
+    B, T, Hq, Hkv = 1, 32768, 28, 4
+    k = synthetic.make_kv(B, T, Hkv, seed=51, theta=1e6, key=True)
+    v = synthetic.make_kv(B, T, Hkv, seed=52, theta=1e6, key=False)
+    q = synthetic.make_q(B, Hq, seed=53)
+    kc, vc = _compress(k), _compress(v)
+    o_c = ekv.decode_attention(q, kc, vc)
+    o_r = kernels.attention_reference(q, k, v, T)
+    assert same_bits(o_c, o_r)
+    _check_close(o_c, q, k, v, T)
+    kernels.check_status()
+
+
+def test_attention_1x128k_raw_pool_stress():
+    """BASELINE config 4 on one GPU: 32 q / 8 kv, 131,072 tokens with 2% forced raw rows,
+    written page by page through the append path into a pool that starts too small
+    (it must grow); compressed == bf16 bit for bit."""
+    B, T, Hq, Hkv = 1, 131072, 32, 8
+    k = synthetic.make_kv(B, T, Hkv, seed=61, theta=1e6, key=True, raw_frac=0.02)
+    v = synthetic.make_kv(B, T, Hkv, seed=62, theta=1e6, key=False, raw_frac=0.02)
+    q = synthetic.make_q(B, Hq, seed=63)
+    T0 = T - 48
+    kc = ekv.CompressedKV(B, T, Hkv, 128, reserve=0.005)
+    vc = ekv.CompressedKV(B, T, Hkv, 128, reserve=0.005)
+    kc.prefill_slot(0, k[:, :T0].contiguous())
+    vc.prefill_slot(0, v[:, :T0].contiguous())
+    for t in range(T0, T):
+        kc.append(k[:, t])
+        vc.append(v[:, t])
+        if kc.T % 16 == 0:
+            ekv.check_overflow([kc, vc])
+    assert kc.grows + vc.grows > 0
+    o_c = ekv.decode_attention(q, kc, vc)
+    o_r = kernels.attention_reference(q, k, v, T)
+    assert same_bits(o_c, o_r)
+    assert same_bits(kernels.decode_to_bf16(kc.buffers(), T), k)
+    kernels.check_status()
