@@ -120,6 +120,27 @@ class CompressedKV:
             if self.T < self.TS:
                 self._open_tail(pg + 1)
 
+    # ------------------------------------------------------------------ device-length steps
+    def append_dev(self, x, T_dev):
+        """Enqueue the append of one token per sequence at the device-side length
+        *T_dev (no host bookkeeping; see kernels.append_token). The host's T is
+        advanced with note_appended() once the step is enqueued."""
+        kernels.append_token(x, self, T_dev)
+
+    def note_appended(self, n=1):
+        self.T += n
+
+    def ensure_headroom(self, pages):
+        """Before `pages` more pages are appended on the device: read the pool
+        counter (one sync) and grow the pool so that even a page of nothing but
+        raw rows always fits. Returns True when the pool moved (work enqueued
+        with the old buffers, such as a captured graph, must be rebuilt)."""
+        need = int(self.cnt.item()) + pages * self.B * self.H * P
+        if need <= self.cap:
+            return False
+        self._grow(need)
+        return True
+
     def finish_page(self, overflowed):
         """Called by check_overflow with this cache's result."""
         if self._pending is not None and overflowed:

@@ -54,6 +54,8 @@ struct AttnArgs {
   float* ws_l;
   int32_t* status;
   int B, TS, NP, Hkv, Hq, G, T;
+  const int32_t* T_dev;         // if set, the valid length is *T_dev + T_add (T is then the capacity)
+  int T_add;
   int ns, split_len, s0, nsl, n_items, ngroups;
   float qk_scale;
 };
@@ -129,14 +131,24 @@ struct Item {
   int b, hg, split, tok0, tok1, page0, npages;
 };
 
-__device__ __forceinline__ Item decode_item(const AttnArgs& a, int item) {
+// Valid tokens of this launch: the host's T, or the device-side length (a
+// launch captured once and replayed while the cache grows), clamped to the
+// capacity the plan was made for.
+__device__ __forceinline__ int valid_tokens(const AttnArgs& a) {
+  if (a.T_dev == nullptr) return a.T;
+  return max(0, min(a.T, *a.T_dev + a.T_add));
+}
+
+// An item whose split lies past T has no pages: its warps write an empty
+// partial (m = -inf, l = 0, o = 0), which the merge weighs with 0.
+__device__ __forceinline__ Item decode_item(const AttnArgs& a, int item, int T) {
   Item it;
   const int bg = item / a.nsl;
   it.split = a.s0 + item % a.nsl;
   it.b = bg / a.ngroups;
   it.hg = bg % a.ngroups;
   it.tok0 = it.split * a.split_len;
-  it.tok1 = min(it.tok0 + a.split_len, a.T);
+  it.tok1 = max(it.tok0, min(it.tok0 + a.split_len, T));
   it.page0 = it.tok0 / kP;
   it.npages = (it.tok1 - it.tok0 + kP - 1) / kP;
   return it;
@@ -638,6 +650,7 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + S);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int Tv = valid_tokens(a);
   if (threadIdx.x == 0) {
     // a merge launched as a programmatic dependent may start its (waiting) CTAs now
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -677,9 +690,11 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
     };
     int item = blockIdx.x, s = 0, nst = 0;
     Item it{};
-    if (item < a.n_items) {
-      it = decode_item(a, item);
+    // the cursor skips items without pages (splits past the valid length)
+    for (; item < a.n_items; item += gridDim.x) {
+      it = decode_item(a, item, Tv);
       nst = (it.npages + WPH - 1) / WPH;
+      if (nst > 0) break;
     }
     int4 md = item < a.n_items ? tile_meta(it, 0) : make_int4(0, 0, 0, 0);
     uint32_t gs = 0;  // stages issued
@@ -751,10 +766,10 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
       ++gs;
       if (++s == nst) {
         s = 0;
-        item += gridDim.x;
-        if (item < a.n_items) {
-          it = decode_item(a, item);
+        for (item += gridDim.x; item < a.n_items; item += gridDim.x) {
+          it = decode_item(a, item, Tv);
           nst = (it.npages + WPH - 1) / WPH;
+          if (nst > 0) break;
         }
       }
       if (item < a.n_items) md = tile_meta(it, s);  // the next stage's metadata, in flight during the wait
@@ -780,7 +795,7 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
   uint32_t qf[NT][16];
 
   for (int item = blockIdx.x; item < a.n_items; item += gridDim.x) {
-    const Item it = decode_item(a, item);
+    const Item it = decode_item(a, item, Tv);
     const int hk = it.hg * HG + hl;
     const int nst = (it.npages + WPH - 1) / WPH;
     load_q<NT>(a, it.b, hk, g, t, qf);
@@ -1047,6 +1062,8 @@ int common_args(AttnArgs& a, const uint16_t* q, int B, int TS, int Hkv, int Hq, 
   a.Hq = Hq;
   a.G = Hq / Hkv;
   a.T = T;
+  a.T_dev = nullptr;
+  a.T_add = 0;
   a.ns = ws->ns;
   a.split_len = ws->split_len;
   a.s0 = s0;
@@ -1121,11 +1138,13 @@ namespace {
 
 int split_compressed(const uint16_t* q, const exk_cview* k, const exk_cview* v, int B, int TS, int Hkv, int Hq, int T,
                      int s0, int s1, const exk_partials* ws, int consumer_warps, float qk_scale, int32_t* status,
-                     int device, void* stream) {
+                     int device, void* stream, const int32_t* T_dev = nullptr, int T_add = 0) {
   if (k == nullptr || v == nullptr) return EXK_EARG;
   AttnArgs a;
   int r = common_args(a, q, B, TS, Hkv, Hq, T, s0, s1, ws, consumer_warps, qk_scale, status);
   if (r != 0) return r;
+  a.T_dev = T_dev;
+  a.T_add = T_add;
   int sms = 0;
   if ((r = use_device(device, &sms)) != 0) return r;
   const int hg = cta_heads(Hkv, consumer_warps);
@@ -1221,6 +1240,19 @@ extern "C" int exk_attention_compressed(const uint16_t* q, const exk_cview* k, c
   if ((reinterpret_cast<uintptr_t>(out) & 7u) != 0) return EXK_EALIGN;
   int r = split_compressed(q, k, v, B, TS, Hkv, Hq, T, 0, ws->ns, ws, consumer_warps, qk_scale, status, device,
                            stream);
+  return r != 0 ? r : launch_merge(ws, B * Hq, out, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int exk_attention_compressed_devlen(const uint16_t* q, const exk_cview* k, const exk_cview* v, int B,
+                                               int TS, int Hkv, int Hq, int T_cap, const int32_t* T_dev, int T_add,
+                                               const exk_partials* ws, uint16_t* out, int consumer_warps,
+                                               float qk_scale, int32_t* status, int device, void* stream) {
+  if (ws == nullptr || out == nullptr || T_dev == nullptr) return EXK_EARG;
+  if ((reinterpret_cast<uintptr_t>(out) & 7u) != 0 || (reinterpret_cast<uintptr_t>(T_dev) & 3u) != 0) return EXK_EALIGN;
+  const int last = (T_cap - 1) / (ws->split_len > 0 ? ws->split_len : 1);
+  if (T_cap <= 0 || last + 1 != ws->ns) return EXK_EARG;  // the plan must be the capacity's
+  int r = split_compressed(q, k, v, B, TS, Hkv, Hq, T_cap, 0, ws->ns, ws, consumer_warps, qk_scale, status, device,
+                           stream, T_dev, T_add);
   return r != 0 ? r : launch_merge(ws, B * Hq, out, static_cast<cudaStream_t>(stream));
 }
 

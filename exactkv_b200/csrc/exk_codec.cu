@@ -35,15 +35,38 @@ struct EncArgs {
   int32_t* cnt;
   int b0, pg0, nb, npg, H, TS, NP;
   int n_ph;
+  // Append mode (one token per step, every launch enqueued once and replayed):
+  // src is the tail area [B, H, 16, 128] at raw row tail_row0, T_dev the
+  // tokens held before this step. encode_kernel first writes app_x[b, h] into
+  // tail row T % 16; when that completes page (T + 1) / 16 - 1 the three
+  // kernels encode it (pg0 comes from T_dev) and raw_copy_kernel opens the
+  // next tail page; otherwise they return at once.
+  const int32_t* T_dev;
+  const uint16_t* app_x;
+  int64_t app_sb, app_sh;
+  int64_t tail_row0;
 };
+
+// First page of this launch: a.pg0, or in append mode the page the step
+// completes (false: the step completes no page, nothing to encode).
+__device__ __forceinline__ bool launch_page(const EncArgs& a, int& pg0) {
+  if (a.T_dev == nullptr) {
+    pg0 = a.pg0;
+    return true;
+  }
+  const int T1 = *a.T_dev + 1;
+  if (T1 % kP != 0 || T1 > a.TS) return false;
+  pg0 = T1 / kP - 1;
+  return true;
+}
 
 // Page-head ph of a launch (ordered sequence, page, head) -> its index in the
 // [B, TS/16, H] page arrays, and its source offset in elements.
-__device__ __forceinline__ int64_t page_index(const EncArgs& a, int ph, int& bi, int& pg, int& hk) {
+__device__ __forceinline__ int64_t page_index(const EncArgs& a, int pg0, int ph, int& bi, int& pg, int& hk) {
   hk = ph % a.H;
   pg = (ph / a.H) % a.npg;
   bi = ph / (a.H * a.npg);
-  return (static_cast<int64_t>(a.b0 + bi) * a.NP + a.pg0 + pg) * a.H + hk;
+  return (static_cast<int64_t>(a.b0 + bi) * a.NP + pg0 + pg) * a.H + hk;
 }
 
 __device__ __forceinline__ uint32_t half_of(const uint32_t (&w)[4], int c) {
@@ -70,9 +93,19 @@ __global__ void __launch_bounds__(kEncWarps * 32) encode_kernel(const __grid_con
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ph = blockIdx.x * kEncWarps + warp;
   if (ph >= a.n_ph) return;  // whole warp
+  if (a.app_x != nullptr) {  // append mode: this warp's (sequence, head) token first
+    const int T = *a.T_dev;
+    if (T >= a.TS) return;
+    const int b = ph / a.H, h = ph % a.H;
+    const uint2 x = reinterpret_cast<const uint2*>(a.app_x + b * a.app_sb + h * a.app_sh)[lane];
+    reinterpret_cast<uint2*>(const_cast<uint16_t*>(a.src) + b * a.s_b + (T % kP) * a.s_p + h * a.s_h)[lane] = x;
+    __syncwarp();  // the page's rows are read below by other lanes
+  }
+  int pg0;
+  if (!launch_page(a, pg0)) return;
   const int q = lane & 15, th = lane >> 4;
   int bi, pg, hk;
-  const int64_t page = page_index(a, ph, bi, pg, hk);
+  const int64_t page = page_index(a, pg0, ph, bi, pg, hk);
 
   uint32_t v[8][4];  // [token][word]: bf16 pairs (4q,4q+1), (4q+2,4q+3), (64+4q, ..), (64+4q+2, ..)
 #pragma unroll
@@ -111,7 +144,7 @@ __global__ void __launch_bounds__(kEncWarps * 32) encode_kernel(const __grid_con
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int tok = th * 8 + i;
-    const int64_t row = (static_cast<int64_t>(a.b0 + bi) * a.TS + (a.pg0 + pg) * kP + tok) * a.H + hk;
+    const int64_t row = (static_cast<int64_t>(a.b0 + bi) * a.TS + (pg0 + pg) * kP + tok) * a.H + hk;
     uint32_t smw[2] = {0u, 0u}, cw = 0u;
     bool esc = false;
 #pragma unroll
@@ -152,6 +185,8 @@ __global__ void __launch_bounds__(kScanThreads) raw_offsets_kernel(const __grid_
   __shared__ int s_warp[kScanThreads / 32];
   __shared__ int s_total;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int pg0;
+  if (!launch_page(a, pg0)) return;  // uniform over the CTA
   int carry = *a.cnt;
   for (int tile = 0; tile < a.n_ph; tile += 4 * kScanThreads) {
     int cnt[4];
@@ -164,7 +199,7 @@ __global__ void __launch_bounds__(kScanThreads) raw_offsets_kernel(const __grid_
       idx[j] = -1;
       if (ph < a.n_ph) {
         int bi, pg, hk;
-        idx[j] = page_index(a, ph, bi, pg, hk);
+        idx[j] = page_index(a, pg0, ph, bi, pg, hk);
         cnt[j] = __popc(static_cast<uint32_t>(a.rowmask[idx[j]]) & 0xFFFFu);
       }
       local += cnt[j];
@@ -208,8 +243,18 @@ __global__ void __launch_bounds__(kEncWarps * 32) raw_copy_kernel(const __grid_c
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ph = blockIdx.x * kEncWarps + warp;
   if (ph >= a.n_ph) return;
+  int pg0;
+  if (!launch_page(a, pg0)) return;
   int bi, pg, hk;
-  const int64_t page = page_index(a, ph, bi, pg, hk);
+  const int64_t page = page_index(a, pg0, ph, bi, pg, hk);
+  if (a.app_x != nullptr && pg0 + 1 < a.NP) {
+    // open the next tail page: all its rows are raw, in this (sequence, head)'s tail rows
+    const int64_t nxt = page + a.H;
+    if (lane == 0) {
+      a.rowmask[nxt] = 0xFFFF;
+      a.rowoff[nxt] = static_cast<int32_t>(a.tail_row0 + static_cast<int64_t>(ph) * kP);
+    }
+  }
   uint32_t rm = static_cast<uint32_t>(a.rowmask[page]) & 0xFFFFu;
   if (rm == 0u) return;
   const int64_t ro = a.rowoff[page];
@@ -331,6 +376,10 @@ extern "C" int exk_encode_pages(const uint16_t* src, int64_t s_b, int64_t s_pg, 
   a.TS = TS;
   a.NP = TS / kP;
   a.n_ph = static_cast<int>(n_ph);
+  a.T_dev = nullptr;
+  a.app_x = nullptr;
+  a.app_sb = a.app_sh = 0;
+  a.tail_row0 = -1;
   const int blocks = static_cast<int>((n_ph + kEncWarps - 1) / kEncWarps);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // 8-byte vector loads need every (sequence, page, token, head) start 8-byte aligned
@@ -379,5 +428,67 @@ extern "C" int exk_decode_to_bf16(const exk_cview* c, int B, int TS, int H, int 
   const int64_t blocks = (a.n_ph + 7) / 8;
   if (blocks > (int64_t{1} << 31) - 1) return EXK_EARG;
   decode_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  return launch_status();
+}
+
+extern "C" int exk_append_token(const uint16_t* x, int64_t x_sb, int64_t x_sh, uint8_t* sm, uint8_t* code,
+                                uint8_t* base, int32_t* rowmask, int32_t* rowoff, uint16_t* raw, int64_t raw_cap,
+                                int32_t* cnt, int B, int H, int TS, const int32_t* T_dev, int32_t* status, int device,
+                                void* stream) {
+  (void)status;
+  if (x == nullptr || sm == nullptr || code == nullptr || base == nullptr || rowmask == nullptr ||
+      rowoff == nullptr || raw == nullptr || cnt == nullptr || T_dev == nullptr)
+    return EXK_EARG;
+  if (B <= 0 || H <= 0 || TS <= 0 || TS % kP != 0 || raw_cap < 0) return EXK_EARG;
+  if (static_cast<int64_t>(B) * H > (int64_t{1} << 30)) return EXK_EARG;
+  if ((reinterpret_cast<uintptr_t>(x) & 7u) != 0 || (x_sb % 4) != 0 || (x_sh % 4) != 0 ||
+      (reinterpret_cast<uintptr_t>(raw) & 7u) != 0 || (reinterpret_cast<uintptr_t>(T_dev) & 3u) != 0)
+    return EXK_EALIGN;
+  int r = use_device(device, nullptr);
+  if (r != 0) return r;
+  EncArgs a;
+  a.src = raw + raw_cap * kD;  // the tail area [B, H, 16, 128]
+  a.s_b = static_cast<int64_t>(H) * kP * kD;
+  a.s_pg = 0;
+  a.s_p = kD;
+  a.s_h = static_cast<int64_t>(kP) * kD;
+  a.sm = sm;
+  a.code = code;
+  a.base = base;
+  a.rowmask = rowmask;
+  a.rowoff = rowoff;
+  a.raw = raw;
+  a.raw_cap = raw_cap;
+  a.cnt = cnt;
+  a.b0 = 0;
+  a.pg0 = 0;
+  a.nb = B;
+  a.npg = 1;
+  a.H = H;
+  a.TS = TS;
+  a.NP = TS / kP;
+  a.n_ph = B * H;
+  a.T_dev = T_dev;
+  a.app_x = x;
+  a.app_sb = x_sb;
+  a.app_sh = x_sh;
+  a.tail_row0 = raw_cap;
+  const int blocks = (a.n_ph + kEncWarps - 1) / kEncWarps;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  encode_kernel<true><<<blocks, kEncWarps * 32, 0, st>>>(a);
+  if ((r = launch_status()) != 0) return r;
+  raw_offsets_kernel<<<1, kScanThreads, 0, st>>>(a);
+  if ((r = launch_status()) != 0) return r;
+  raw_copy_kernel<true><<<blocks, kEncWarps * 32, 0, st>>>(a);
+  return launch_status();
+}
+
+__global__ void advance_kernel(int32_t* T_dev, int n) { *T_dev += n; }
+
+extern "C" int exk_advance_length(int32_t* T_dev, int n, int device, void* stream) {
+  if (T_dev == nullptr) return EXK_EARG;
+  int r = use_device(device, nullptr);
+  if (r != 0) return r;
+  advance_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(T_dev, n);
   return launch_status();
 }

@@ -228,3 +228,51 @@ def encode_pages(src, strides, buf, b0, pg0, nb, npg):
                               b0, pg0, nb, npg, buf["H"], buf["TS"], status_tensor(dev.index).data_ptr(),
                               dev.index, stream)
     check(rc, "exk_encode_pages")
+
+
+# ----------------------------------------------------------------------------- device-length decode steps
+#
+# One decode step whose token count lives on the device (an int32 tensor, the
+# tokens held before the step), so the whole step can be enqueued once and
+# replayed (CUDA graphs): append_token writes and, at page boundaries, encodes;
+# attention_compressed_devlen reads T from the device with the plan for the
+# caches' capacity; advance_length moves the count on. No host synchronisation.
+
+def append_token(x, c, T_dev):
+    """x [B, H, 128] bf16 (channels contiguous): the step's token for every
+    sequence of CompressedKV `c`, appended at row *T_dev."""
+    if x.dtype != torch.bfloat16 or x.stride(-1) != 1 or tuple(x.shape) != (c.B, c.H, D):
+        raise ValueError("x must be bf16 [B, H, 128] with contiguous channels")
+    dev = x.device
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    rc = lib.exk_append_token(x.data_ptr(), x.stride(0), x.stride(1), c.sm.data_ptr(), c.code.data_ptr(),
+                              c.base.data_ptr(), c.rowmask.data_ptr(), c.rowoff.data_ptr(), c.raw.data_ptr(), c.cap,
+                              c.cnt.data_ptr(), c.B, c.H, c.TS, T_dev.data_ptr(), status_tensor(dev.index).data_ptr(),
+                              dev.index, stream)
+    check(rc, "exk_append_token")
+
+
+def advance_length(T_dev, n=1):
+    dev = T_dev.device
+    check(lib.exk_advance_length(T_dev.data_ptr(), n, dev.index, torch.cuda.current_stream(dev).cuda_stream),
+          "exk_advance_length")
+
+
+def attention_compressed_devlen(q, kc, vc, T_dev, T_add=1, out=None, num_warps=None):
+    """Decode attention over the first min(TS, *T_dev + T_add) tokens of the caches,
+    with the split plan for their capacity TS (see exk_attention_compressed_devlen)."""
+    ka, TS, Hkv = _cache_args(kc)
+    va, _, _ = _cache_args(vc)
+    _check_q(q, TS, TS)
+    B, Hq, _ = q.shape
+    dev = q.device.index
+    stream = torch.cuda.current_stream(q.device).cuda_stream
+    ns, sl = plan_splits(B, Hkv, TS, dev)
+    ws = _workspace(q.device, stream, B * Hq, ns, sl)
+    out = torch.empty_like(q) if out is None else out
+    rc = lib.exk_attention_compressed_devlen(q.data_ptr(), ctypes.byref(ka), ctypes.byref(va), B, TS, Hkv, Hq, TS,
+                                             T_dev.data_ptr(), T_add, ctypes.byref(ws[3]), out.data_ptr(),
+                                             _consumer_warps(num_warps), D ** -0.5 * LOG2E,
+                                             status_tensor(dev).data_ptr(), dev, stream)
+    check(rc, "exk_attention_compressed_devlen")
+    return out
