@@ -26,9 +26,12 @@ reasons are sampled through NVML every 5 ms during warm-up and timing.
 
 e2e: the same metric through the public API with host buffers: each step
 copies q [B, Hq, 128] and the new token's K and V [B, Hkv, 128] from pinned
-host memory, appends them to the caches (encoding a page every 16 steps,
-with the check_overflow sync), runs decode_attention and copies the output
-back to pinned host memory; the context grows by one token per step.
+host memory into the step's device buffers, replays a captured CUDA graph of
+the device-length decode step (exactkv_b200.graph: append, page encode at
+page boundaries, decode attention, length advance; the raw pools are kept
+ahead with one host sync per 8 pages instead of a sync per page) and copies
+the output back to pinned host memory; the context grows by one token per
+step.
 
 engine: BASELINE configs[4] decode throughput through exactkv_b200.Engine on a
 random-init Llama-3.1-8B (32 layers, hidden 4096, 32 q / 8 kv heads, FFN 14336,
@@ -374,19 +377,51 @@ def time_encoder(kbf, B, T, Hkv, dev, reps=5):
 
 
 def run_e2e(a, kc, vc, B, Hq, Hkv, T0, dev, world, raw_rows0, ns0):
-    """Public-API decode steps with host buffers (see module docstring)."""
+    """Public-API decode steps with host buffers (see module docstring): each step
+    copies its inputs from pinned host memory, replays the captured device-length
+    step (exactkv_b200.graph) and copies the output back to pinned memory."""
     import torch
     import torch.distributed as dist
 
     import exactkv_b200 as ekv
+    from exactkv_b200 import kernels
+    from exactkv_b200.graph import DeviceLength, GraphedStep
 
     K = a.steps
     g = torch.Generator().manual_seed(77)
-    q_h = torch.randn(K, B, Hq, 128, generator=g).to(torch.bfloat16).pin_memory()
-    k_h = torch.randn(K, B, Hkv, 128, generator=g).to(torch.bfloat16).pin_memory()
-    v_h = torch.randn(K, B, Hkv, 128, generator=g).to(torch.bfloat16).pin_memory()
-    o_h = torch.empty(K, B, Hq, 128, dtype=torch.bfloat16).pin_memory()
+    n_all = K + 2
+    nq, nk = B * Hq * 128, B * Hkv * 128
+    # one pinned row per step: q, the new K token, the new V token (one H2D copy per step)
+    inp_h = torch.randn(n_all, nq + 2 * nk, generator=g).to(torch.bfloat16).pin_memory()
+    o_h = torch.empty(n_all, B, Hq, 128, dtype=torch.bfloat16).pin_memory()
     stream = torch.cuda.current_stream(dev)
+    side = torch.cuda.Stream(dev)
+    length = DeviceLength([kc, vc])
+    inp = torch.empty(nq + 2 * nk, dtype=torch.bfloat16, device=dev)
+    q_in = inp[:nq].view(B, Hq, 128)
+    k_in = inp[nq:nq + nk].view(B, Hkv, 128)
+    v_in = inp[nq + nk:].view(B, Hkv, 128)
+    out = torch.empty_like(q_in)
+
+    def body():
+        main = torch.cuda.current_stream(dev)
+        side.wait_stream(main)
+        with torch.cuda.stream(side):             # the two caches' appends overlap
+            vc.append_dev(v_in, length.t)
+        kc.append_dev(k_in, length.t)
+        main.wait_stream(side)
+        kernels.attention_compressed_devlen(q_in, kc, vc, length.t, 1, out=out, advance=1)
+
+    gs = GraphedStep(body, length, check_pages=8)
+    ns_cap, _ = kernels.plan_splits(B, Hkv, kc.TS, dev)
+
+    def one(i):
+        inp.copy_(inp_h[i], non_blocking=True)
+        gs.step()
+        o_h[i].copy_(out, non_blocking=True)      # device -> host read of the step's result
+
+    for i in range(2):                            # untimed: the first step captures the graph
+        one(K + i)
     nbytes_total = 0
     if world > 1:
         dist.barrier()
@@ -396,23 +431,19 @@ def run_e2e(a, kc, vc, B, Hq, Hkv, T0, dev, world, raw_rows0, ns0):
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for i in range(K):
-        q = q_h[i].to(dev, non_blocking=True)
-        kc.append(k_h[i].to(dev, non_blocking=True))
-        vc.append(v_h[i].to(dev, non_blocking=True))
-        if kc.T % 16 == 0:
-            ekv.check_overflow([kc, vc])
-        o = ekv.decode_attention(q, kc, vc)
-        o_h[i].copy_(o, non_blocking=True)        # device -> host read of the step's result (pinned, on the stream)
+        one(i)
         T = kc.T
         npt = -(-T // 16)
         # as algorithmic_bytes(): full-page rows, page metadata, the prefill's raw rows and the
         # raw tail rows (pages encoded during these steps add a few more raw rows, not counted)
         nbytes_total += (2 * (B * npt * 16 * Hkv * 192 + B * npt * Hkv * 136)
-                         + (raw_rows0 + 2 * B * Hkv * (T % 16)) * 256 + B * Hq * 256 + B * Hq * ns0 * 520)
+                         + (raw_rows0 + 2 * B * Hkv * (T % 16)) * 256 + B * Hq * 256 + B * Hq * ns_cap * 520)
     e1.record(stream)
     torch.cuda.synchronize(dev)
     wall = time.perf_counter() - t0
     ms = e0.elapsed_time(e1)
+    gs.close()
+    kernels.check_status(dev)
     t = torch.tensor([ms], device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -421,9 +452,10 @@ def run_e2e(a, kc, vc, B, Hq, Hkv, T0, dev, world, raw_rows0, ns0):
     d2h = B * Hq * 128 * 2
     return {"value": round(nbytes_total * world / (ms * 1e-3) / 1e12, 4), "unit": UNIT,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms / K, 4),
-            "wall_ms_per_step": round(wall / K * 1e3, 4),
-            "what": "per step: H2D q + new K/V token (pinned), append (+page encode / check_overflow every 16, "
-                    "which syncs), decode_attention, D2H output into pinned memory on the stream; "
+            "wall_ms_per_step": round(wall / K * 1e3, 4), "graph_captures": gs.captures,
+            "what": "per step: H2D q + new K/V token from pinned memory, a replayed CUDA graph of the "
+                    "device-length step (append + page encode at boundaries, decode attention, length advance; "
+                    "pools kept ahead with one sync per 8 pages), D2H output into pinned memory; "
                     "context grows from 4096"}
 
 

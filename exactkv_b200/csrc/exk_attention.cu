@@ -982,11 +982,13 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
 
 __global__ void __launch_bounds__(128) merge_kernel(const float* __restrict__ o, const float* __restrict__ m,
                                                     const float* __restrict__ l, int ns, int rows,
-                                                    uint16_t* __restrict__ out) {
+                                                    uint16_t* __restrict__ out, int32_t* advance, int n_adv) {
   // Launched as a programmatic dependent of the split kernel: the CTAs may be
   // resident early; this waits until the split grid has finished and its
   // partials are visible (a no-op after an ordinary launch).
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  // a device-length step ends here: the split kernel has read the length
+  if (advance != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *advance += n_adv;
   const int row = blockIdx.x * 4 + (threadIdx.x >> 5);
   if (row >= rows) return;
   merge_row(o, m, l, ns, row, threadIdx.x & 31, out);
@@ -1200,7 +1202,8 @@ int split_bf16(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, i
 
 // Merge launch: a programmatic dependent of the preceding kernel on the stream
 // (its CTAs are scheduled early and wait in griddepcontrol.wait).
-int launch_merge(const exk_partials* ws, int rows, uint16_t* out, cudaStream_t stream) {
+int launch_merge(const exk_partials* ws, int rows, uint16_t* out, cudaStream_t stream, int32_t* advance = nullptr,
+                 int n_adv = 0) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((rows + 3) / 4);
   cfg.blockDim = dim3(128);
@@ -1213,7 +1216,7 @@ int launch_merge(const exk_partials* ws, int rows, uint16_t* out, cudaStream_t s
   cfg.numAttrs = 1;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, merge_kernel, static_cast<const float*>(ws->o),
                                            static_cast<const float*>(ws->m), static_cast<const float*>(ws->l), ws->ns,
-                                           rows, out);
+                                           rows, out, advance, n_adv);
   return e == cudaSuccess ? 0 : static_cast<int>(e);
 }
 
@@ -1244,16 +1247,18 @@ extern "C" int exk_attention_compressed(const uint16_t* q, const exk_cview* k, c
 }
 
 extern "C" int exk_attention_compressed_devlen(const uint16_t* q, const exk_cview* k, const exk_cview* v, int B,
-                                               int TS, int Hkv, int Hq, int T_cap, const int32_t* T_dev, int T_add,
-                                               const exk_partials* ws, uint16_t* out, int consumer_warps,
-                                               float qk_scale, int32_t* status, int device, void* stream) {
+                                               int TS, int Hkv, int Hq, int T_cap, int32_t* T_dev, int T_add,
+                                               int advance, const exk_partials* ws, uint16_t* out,
+                                               int consumer_warps, float qk_scale, int32_t* status, int device,
+                                               void* stream) {
   if (ws == nullptr || out == nullptr || T_dev == nullptr) return EXK_EARG;
   if ((reinterpret_cast<uintptr_t>(out) & 7u) != 0 || (reinterpret_cast<uintptr_t>(T_dev) & 3u) != 0) return EXK_EALIGN;
   const int last = (T_cap - 1) / (ws->split_len > 0 ? ws->split_len : 1);
   if (T_cap <= 0 || last + 1 != ws->ns) return EXK_EARG;  // the plan must be the capacity's
   int r = split_compressed(q, k, v, B, TS, Hkv, Hq, T_cap, 0, ws->ns, ws, consumer_warps, qk_scale, status, device,
                            stream, T_dev, T_add);
-  return r != 0 ? r : launch_merge(ws, B * Hq, out, static_cast<cudaStream_t>(stream));
+  return r != 0 ? r : launch_merge(ws, B * Hq, out, static_cast<cudaStream_t>(stream), advance ? T_dev : nullptr,
+                                   advance);
 }
 
 extern "C" int exk_attention_bf16(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int TS, int Hkv,

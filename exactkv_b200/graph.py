@@ -41,8 +41,10 @@ class DeviceLength:
 
 class GraphedStep:
     """step(): replays `body` — a function that enqueues one decode step on the
-    current stream using `length.t` and ends with length.advance() — from a
-    CUDA graph. The first call, and any call after a pool grew, captures it."""
+    current stream using `length.t` and ends by advancing it (length.advance(),
+    or attention_compressed_devlen(..., advance=1)); it may fork work onto other
+    streams that join the current one — from a CUDA graph. The first call, and
+    any call after a pool grew, captures it."""
 
     def __init__(self, body, length, check_pages=8):
         self.body, self.length, self.check_pages = body, length, check_pages

@@ -258,9 +258,10 @@ def advance_length(T_dev, n=1):
           "exk_advance_length")
 
 
-def attention_compressed_devlen(q, kc, vc, T_dev, T_add=1, out=None, num_warps=None):
+def attention_compressed_devlen(q, kc, vc, T_dev, T_add=1, out=None, num_warps=None, advance=0):
     """Decode attention over the first min(TS, *T_dev + T_add) tokens of the caches,
-    with the split plan for their capacity TS (see exk_attention_compressed_devlen)."""
+    with the split plan for their capacity TS (see exk_attention_compressed_devlen);
+    advance != 0 then adds it to *T_dev on the device (the end of a step)."""
     ka, TS, Hkv = _cache_args(kc)
     va, _, _ = _cache_args(vc)
     _check_q(q, TS, TS)
@@ -271,7 +272,7 @@ def attention_compressed_devlen(q, kc, vc, T_dev, T_add=1, out=None, num_warps=N
     ws = _workspace(q.device, stream, B * Hq, ns, sl)
     out = torch.empty_like(q) if out is None else out
     rc = lib.exk_attention_compressed_devlen(q.data_ptr(), ctypes.byref(ka), ctypes.byref(va), B, TS, Hkv, Hq, TS,
-                                             T_dev.data_ptr(), T_add, ctypes.byref(ws[3]), out.data_ptr(),
+                                             T_dev.data_ptr(), T_add, advance, ctypes.byref(ws[3]), out.data_ptr(),
                                              _consumer_warps(num_warps), D ** -0.5 * LOG2E,
                                              status_tensor(dev).data_ptr(), dev, stream)
     check(rc, "exk_attention_compressed_devlen")

@@ -123,11 +123,12 @@ int exk_attention_compressed(const uint16_t *q, const exk_cview *k, const exk_cv
  * T = min(T_cap, *T_dev + T_add), so one enqueued call (e.g. inside a captured
  * CUDA graph) serves every step of a growing cache. `ws` must hold the plan for
  * T_cap (its splits exactly cover T_cap); splits past T contribute nothing.
- * Same results as exk_attention_compressed with that plan at length T. No
- * counterpart in the reference (its calls take T on the host). */
+ * Same results as exk_attention_compressed with that plan at length T. With
+ * advance != 0 the merge then adds `advance` to *T_dev (the end of a step).
+ * No counterpart in the reference (its calls take T on the host). */
 int exk_attention_compressed_devlen(const uint16_t *q, const exk_cview *k, const exk_cview *v,
-                                    int B, int TS, int Hkv, int Hq, int T_cap, const int32_t *T_dev,
-                                    int T_add, const exk_partials *ws, uint16_t *out,
+                                    int B, int TS, int Hkv, int Hq, int T_cap, int32_t *T_dev,
+                                    int T_add, int advance, const exk_partials *ws, uint16_t *out,
                                     int consumer_warps, float qk_scale, int32_t *status, int device,
                                     void *stream);
 
