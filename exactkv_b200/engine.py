@@ -7,7 +7,8 @@ The model's own modules do everything except the cache and the decode
 attention, so an engine on CompressedKV and one on BF16KV compute identical
 logits (the compressed cache is lossless and the two attention kernels are
 bit-identical). Prefill runs the model's forward pass one sequence at a time
-and copies its keys/values into the caches; all sequences share one prompt
+and encodes its keys/values straight from the model's [1, H, T, D] cache
+layout (strided reads, no transposed copy); all sequences share one prompt
 length (as in the reference).
 """
 import torch
@@ -81,8 +82,9 @@ class Engine:
             out = self.m.model(ids[b:b + 1], use_cache=True)
             for i, (kc, vc) in enumerate(self.kv):
                 k, v = self._layer_kv(out.past_key_values, i)
-                kc.prefill_slot(b, k.transpose(1, 2).contiguous())
-                vc.prefill_slot(b, v.transpose(1, 2).contiguous())
+                # the encoder reads the HF layout [1, H, T, D] through strides: no transposed copy
+                kc.prefill_slot(b, k.transpose(1, 2))
+                vc.prefill_slot(b, v.transpose(1, 2))
             nxt[b] = self._logits(out.last_hidden_state[:, -1]).argmax(-1)[0]
             del out
         return nxt

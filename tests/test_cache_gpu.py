@@ -67,3 +67,20 @@ def test_bits_per_value_and_nbytes():
     x = torch.randn(1, 64, 2, 128).to(torch.bfloat16).cuda()
     enc = ekv.encode_reference(x)
     assert 12.5 <= ekv.bits_per_value(enc) < 13.5
+
+
+def test_prefill_from_hf_layout_view():
+    """Prefill straight from a model's [1, H, T, D] cache through a transposed view
+    (the encoder reads it by strides) writes the same bytes as from a contiguous
+    [1, T, H, D] copy."""
+    from exactkv_b200 import synthetic
+    T, H = 1000, 4
+    x = synthetic.make_kv(2, T, H, seed=81, key=True)                 # [B, T, H, D]
+    hf = x.transpose(1, 2).contiguous()                               # [B, H, T, D], as HF stores it
+    a = ekv.CompressedKV(2, 1024, H, 128)
+    b = ekv.CompressedKV(2, 1024, H, 128)
+    for s in range(2):
+        a.prefill_slot(s, x[s:s + 1].contiguous())
+        b.prefill_slot(s, hf[s:s + 1].transpose(1, 2))
+    for f in ("sm", "code", "base", "rowmask", "rowoff", "raw", "cnt"):
+        assert torch.equal(getattr(a, f), getattr(b, f)), f
