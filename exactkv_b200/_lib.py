@@ -45,10 +45,13 @@ _SIGNATURES.update({
                                  c_int, c_int, c_int, c_void_p, c_int, c_void_p]),
     "exk_decode_to_bf16": (c_int, [_P(CView), c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_void_p]),
     "exk_attention_compressed_devlen": (c_int, [c_void_p, _P(CView), _P(CView), c_int, c_int, c_int, c_int, c_int,
-                                                c_void_p, c_int, c_int, _P(Partials), c_void_p, c_int, c_float,
+                                                c_void_p, c_int, c_int, c_int, _P(Partials), c_void_p, c_int, c_float,
                                                 c_void_p, c_int, c_void_p]),
+    "exk_attention_bf16_devlen": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
+                                          c_void_p, c_int, c_int, c_int, _P(Partials), c_void_p, c_int, c_float,
+                                          c_void_p, c_int, c_void_p]),
     "exk_append_token": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
-                                 c_void_p, c_int64, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_int,
+                                 c_void_p, c_int64, c_void_p, c_int, c_int, c_int, c_void_p, c_int, c_void_p, c_int,
                                  c_void_p]),
     "exk_advance_length": (c_int, [c_void_p, c_int, c_int, c_void_p]),
     "exk_attention_compressed_noalloc": (c_int, [c_void_p, _P(CView), _P(CView), c_int, c_int, c_int, c_int, c_int,

@@ -36,6 +36,7 @@ class CompressedKV:
         self.cap = max(64, int(B * TS * H * reserve))
         self.raw = torch.zeros(self.cap + B * H * P, D, dtype=torch.bfloat16, device=device)
         self.T = 0
+        self.lens = [0] * B                     # tokens per sequence (all equal unless filled slot by slot)
         self.grows = 0
         self._pending = None                    # (strides, page) waiting for check_overflow
         self._rebind()
@@ -74,8 +75,9 @@ class CompressedKV:
         self.raw, self.cap = raw, new_cap
         self.grows += 1
         self._rebind()
-        if self.T < self.TS:
-            self.rowoff[:, self.T // P] = self._toff     # the open tail page moved with the pool
+        for b, t in enumerate(self.lens):                   # every open tail page moved with the pool
+            if t < self.TS:
+                self.rowoff[b, t // P] = self._toff[b]
 
     def _encode(self, src, strides, b0, pg0, nb, npg):
         self._before.copy_(self.cnt)
@@ -93,15 +95,19 @@ class CompressedKV:
 
     # ------------------------------------------------------------------ interface
     def prefill_slot(self, b, x):
-        """x: [1, T, H, D] bf16 for sequence slot b. All slots must have the same T."""
+        """x: [1, T, H, D] bf16 (any strides, channels contiguous) for sequence slot b.
+        The host-side append path needs every slot at the same T; slots of different
+        lengths (a variable-length batch) are served by the device-length calls."""
         T = x.shape[1]
         full = T // P * P
+        self.lens[b] = T
         if full:
             st = (x.stride(0), P * x.stride(1), x.stride(1), x.stride(2))
             self._encode(x, st, b, 0, 1, full // P)
             self._redo(x, st, b, 0, 1, full // P)          # one sync per prefilled sequence
-        if full < self.TS and b == 0:
-            self._open_tail(full // P)
+        if full < self.TS:                                 # this slot's open tail page
+            self.rowmask[b, full // P] = (1 << P) - 1
+            self.rowoff[b, full // P] = self._toff[b]
         self._tailv[b, :, : T - full] = x[0, full:].transpose(0, 1)
         self.T = T
 
@@ -111,6 +117,7 @@ class CompressedKV:
             raise RuntimeError("call check_overflow() after a page boundary before appending again")
         self._tailv[:, :, self.T % P] = x
         self.T += 1
+        self.lens = [self.T] * self.B
         if self.T % P == 0:
             pg = self.T // P - 1
             t = self._tailv
@@ -129,6 +136,12 @@ class CompressedKV:
 
     def note_appended(self, n=1):
         self.T += n
+        self.lens = [t + n for t in self.lens]
+
+    def lengths(self):
+        """The sequences' token counts as a device int32 tensor (the T_dev of a
+        variable-length batch for the device-length calls)."""
+        return torch.tensor(self.lens, dtype=torch.int32, device=self.dev)
 
     def ensure_headroom(self, pages):
         """Before `pages` more pages are appended on the device: read the pool

@@ -54,8 +54,8 @@ struct AttnArgs {
   float* ws_l;
   int32_t* status;
   int B, TS, NP, Hkv, Hq, G, T;
-  const int32_t* T_dev;         // if set, the valid length is *T_dev + T_add (T is then the capacity)
-  int T_add;
+  const int32_t* T_dev;         // if set, sequence b's valid length is T_dev[b * T_stride] + T_add
+  int T_add, T_stride;          // (T is then the capacity; T_stride 0: one length for the batch)
   int ns, split_len, s0, nsl, n_items, ngroups;
   float qk_scale;
 };
@@ -134,19 +134,20 @@ struct Item {
 // Valid tokens of this launch: the host's T, or the device-side length (a
 // launch captured once and replayed while the cache grows), clamped to the
 // capacity the plan was made for.
-__device__ __forceinline__ int valid_tokens(const AttnArgs& a) {
+__device__ __forceinline__ int valid_tokens(const AttnArgs& a, int b) {
   if (a.T_dev == nullptr) return a.T;
-  return max(0, min(a.T, *a.T_dev + a.T_add));
+  return max(0, min(a.T, a.T_dev[static_cast<int64_t>(b) * a.T_stride] + a.T_add));
 }
 
-// An item whose split lies past T has no pages: its warps write an empty
-// partial (m = -inf, l = 0, o = 0), which the merge weighs with 0.
-__device__ __forceinline__ Item decode_item(const AttnArgs& a, int item, int T) {
+// An item whose split lies past its sequence's length has no pages: its warps
+// write an empty partial (m = -inf, l = 0, o = 0), which the merge weighs with 0.
+__device__ __forceinline__ Item decode_item(const AttnArgs& a, int item) {
   Item it;
   const int bg = item / a.nsl;
   it.split = a.s0 + item % a.nsl;
   it.b = bg / a.ngroups;
   it.hg = bg % a.ngroups;
+  const int T = valid_tokens(a, it.b);
   it.tok0 = it.split * a.split_len;
   it.tok1 = max(it.tok0, min(it.tok0 + a.split_len, T));
   it.page0 = it.tok0 / kP;
@@ -650,7 +651,6 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + S);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int Tv = valid_tokens(a);
   if (threadIdx.x == 0) {
     // a merge launched as a programmatic dependent may start its (waiting) CTAs now
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -692,7 +692,7 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
     Item it{};
     // the cursor skips items without pages (splits past the valid length)
     for (; item < a.n_items; item += gridDim.x) {
-      it = decode_item(a, item, Tv);
+      it = decode_item(a, item);
       nst = (it.npages + WPH - 1) / WPH;
       if (nst > 0) break;
     }
@@ -767,7 +767,7 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
       if (++s == nst) {
         s = 0;
         for (item += gridDim.x; item < a.n_items; item += gridDim.x) {
-          it = decode_item(a, item, Tv);
+          it = decode_item(a, item);
           nst = (it.npages + WPH - 1) / WPH;
           if (nst > 0) break;
         }
@@ -795,7 +795,7 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
   uint32_t qf[NT][16];
 
   for (int item = blockIdx.x; item < a.n_items; item += gridDim.x) {
-    const Item it = decode_item(a, item, Tv);
+    const Item it = decode_item(a, item);
     const int hk = it.hg * HG + hl;
     const int nst = (it.npages + WPH - 1) / WPH;
     load_q<NT>(a, it.b, hk, g, t, qf);
@@ -1066,6 +1066,7 @@ int common_args(AttnArgs& a, const uint16_t* q, int B, int TS, int Hkv, int Hq, 
   a.T = T;
   a.T_dev = nullptr;
   a.T_add = 0;
+  a.T_stride = 0;
   a.ns = ws->ns;
   a.split_len = ws->split_len;
   a.s0 = s0;
@@ -1140,13 +1141,14 @@ namespace {
 
 int split_compressed(const uint16_t* q, const exk_cview* k, const exk_cview* v, int B, int TS, int Hkv, int Hq, int T,
                      int s0, int s1, const exk_partials* ws, int consumer_warps, float qk_scale, int32_t* status,
-                     int device, void* stream, const int32_t* T_dev = nullptr, int T_add = 0) {
+                     int device, void* stream, const int32_t* T_dev = nullptr, int T_add = 0, int T_stride = 0) {
   if (k == nullptr || v == nullptr) return EXK_EARG;
   AttnArgs a;
   int r = common_args(a, q, B, TS, Hkv, Hq, T, s0, s1, ws, consumer_warps, qk_scale, status);
   if (r != 0) return r;
   a.T_dev = T_dev;
   a.T_add = T_add;
+  a.T_stride = T_stride;
   int sms = 0;
   if ((r = use_device(device, &sms)) != 0) return r;
   const int hg = cta_heads(Hkv, consumer_warps);
@@ -1178,11 +1180,14 @@ int split_compressed(const uint16_t* q, const exk_cview* k, const exk_cview* v, 
 
 int split_bf16(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int TS, int Hkv, int Hq, int T, int s0,
                int s1, const exk_partials* ws, int consumer_warps, float qk_scale, int32_t* status, int device,
-               void* stream) {
+               void* stream, const int32_t* T_dev = nullptr, int T_add = 0, int T_stride = 0) {
   if (k == nullptr || v == nullptr) return EXK_EARG;
   AttnArgs a;
   int r = common_args(a, q, B, TS, Hkv, Hq, T, s0, s1, ws, consumer_warps, qk_scale, status);
   if (r != 0) return r;
+  a.T_dev = T_dev;
+  a.T_add = T_add;
+  a.T_stride = T_stride;
   int sms = 0;
   if ((r = use_device(device, &sms)) != 0) return r;
   if (!aligned16(k) || !aligned16(v)) return EXK_EALIGN;
@@ -1246,17 +1251,38 @@ extern "C" int exk_attention_compressed(const uint16_t* q, const exk_cview* k, c
   return r != 0 ? r : launch_merge(ws, B * Hq, out, static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int exk_attention_compressed_devlen(const uint16_t* q, const exk_cview* k, const exk_cview* v, int B,
-                                               int TS, int Hkv, int Hq, int T_cap, int32_t* T_dev, int T_add,
-                                               int advance, const exk_partials* ws, uint16_t* out,
-                                               int consumer_warps, float qk_scale, int32_t* status, int device,
-                                               void* stream) {
-  if (ws == nullptr || out == nullptr || T_dev == nullptr) return EXK_EARG;
+// Checks shared by the device-length entries.
+int devlen_args(const exk_partials* ws, const uint16_t* out, const int32_t* T_dev, int T_cap, int T_stride,
+                int advance) {
+  if (ws == nullptr || out == nullptr || T_dev == nullptr || (T_stride != 0 && T_stride != 1)) return EXK_EARG;
+  if (advance != 0 && T_stride != 0) return EXK_EARG;  // only a batch-wide length is advanced by the merge
   if ((reinterpret_cast<uintptr_t>(out) & 7u) != 0 || (reinterpret_cast<uintptr_t>(T_dev) & 3u) != 0) return EXK_EALIGN;
   const int last = (T_cap - 1) / (ws->split_len > 0 ? ws->split_len : 1);
   if (T_cap <= 0 || last + 1 != ws->ns) return EXK_EARG;  // the plan must be the capacity's
-  int r = split_compressed(q, k, v, B, TS, Hkv, Hq, T_cap, 0, ws->ns, ws, consumer_warps, qk_scale, status, device,
-                           stream, T_dev, T_add);
+  return 0;
+}
+
+extern "C" int exk_attention_compressed_devlen(const uint16_t* q, const exk_cview* k, const exk_cview* v, int B,
+                                               int TS, int Hkv, int Hq, int T_cap, int32_t* T_dev, int T_add,
+                                               int T_stride, int advance, const exk_partials* ws, uint16_t* out,
+                                               int consumer_warps, float qk_scale, int32_t* status, int device,
+                                               void* stream) {
+  int r = devlen_args(ws, out, T_dev, T_cap, T_stride, advance);
+  if (r != 0) return r;
+  r = split_compressed(q, k, v, B, TS, Hkv, Hq, T_cap, 0, ws->ns, ws, consumer_warps, qk_scale, status, device,
+                       stream, T_dev, T_add, T_stride);
+  return r != 0 ? r : launch_merge(ws, B * Hq, out, static_cast<cudaStream_t>(stream), advance ? T_dev : nullptr,
+                                   advance);
+}
+
+extern "C" int exk_attention_bf16_devlen(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int TS,
+                                         int Hkv, int Hq, int T_cap, int32_t* T_dev, int T_add, int T_stride,
+                                         int advance, const exk_partials* ws, uint16_t* out, int consumer_warps,
+                                         float qk_scale, int32_t* status, int device, void* stream) {
+  int r = devlen_args(ws, out, T_dev, T_cap, T_stride, advance);
+  if (r != 0) return r;
+  r = split_bf16(q, k, v, B, TS, Hkv, Hq, T_cap, 0, ws->ns, ws, consumer_warps, qk_scale, status, device, stream,
+                 T_dev, T_add, T_stride);
   return r != 0 ? r : launch_merge(ws, B * Hq, out, static_cast<cudaStream_t>(stream), advance ? T_dev : nullptr,
                                    advance);
 }

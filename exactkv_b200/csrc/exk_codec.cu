@@ -41,24 +41,36 @@ struct EncArgs {
   // tail row T % 16; when that completes page (T + 1) / 16 - 1 the three
   // kernels encode it (pg0 comes from T_dev) and raw_copy_kernel opens the
   // next tail page; otherwise they return at once.
+  // With T_stride 1 every sequence has its own length T_dev[b] (a
+  // variable-length batch): each sequence appends at its own row and
+  // completes its pages on its own steps.
   const int32_t* T_dev;
+  int T_stride;
   const uint16_t* app_x;
   int64_t app_sb, app_sh;
   int64_t tail_row0;
 };
 
-// First page of this launch: a.pg0, or in append mode the page the step
-// completes (false: the step completes no page, nothing to encode).
-__device__ __forceinline__ bool launch_page(const EncArgs& a, int& pg0) {
+// Tokens sequence b holds before this step (append mode).
+__device__ __forceinline__ int step_length(const EncArgs& a, int b) {
+  return a.T_dev[static_cast<int64_t>(b) * a.T_stride];
+}
+
+// First page of sequence b in this launch: a.pg0, or in append mode the page
+// the step completes (false: the step completes no page of b).
+__device__ __forceinline__ bool launch_page(const EncArgs& a, int b, int& pg0) {
   if (a.T_dev == nullptr) {
     pg0 = a.pg0;
     return true;
   }
-  const int T1 = *a.T_dev + 1;
+  const int T1 = step_length(a, b) + 1;
   if (T1 % kP != 0 || T1 > a.TS) return false;
   pg0 = T1 / kP - 1;
   return true;
 }
+
+// Sequence (launch-relative) of page-head ph.
+__device__ __forceinline__ int seq_of(const EncArgs& a, int ph) { return ph / (a.H * a.npg); }
 
 // Page-head ph of a launch (ordered sequence, page, head) -> its index in the
 // [B, TS/16, H] page arrays, and its source offset in elements.
@@ -94,15 +106,15 @@ __global__ void __launch_bounds__(kEncWarps * 32) encode_kernel(const __grid_con
   const int ph = blockIdx.x * kEncWarps + warp;
   if (ph >= a.n_ph) return;  // whole warp
   if (a.app_x != nullptr) {  // append mode: this warp's (sequence, head) token first
-    const int T = *a.T_dev;
-    if (T >= a.TS) return;
     const int b = ph / a.H, h = ph % a.H;
+    const int T = step_length(a, b);
+    if (T >= a.TS) return;
     const uint2 x = reinterpret_cast<const uint2*>(a.app_x + b * a.app_sb + h * a.app_sh)[lane];
     reinterpret_cast<uint2*>(const_cast<uint16_t*>(a.src) + b * a.s_b + (T % kP) * a.s_p + h * a.s_h)[lane] = x;
     __syncwarp();  // the page's rows are read below by other lanes
   }
   int pg0;
-  if (!launch_page(a, pg0)) return;
+  if (!launch_page(a, a.b0 + seq_of(a, ph), pg0)) return;
   const int q = lane & 15, th = lane >> 4;
   int bi, pg, hk;
   const int64_t page = page_index(a, pg0, ph, bi, pg, hk);
@@ -185,8 +197,8 @@ __global__ void __launch_bounds__(kScanThreads) raw_offsets_kernel(const __grid_
   __shared__ int s_warp[kScanThreads / 32];
   __shared__ int s_total;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  int pg0;
-  if (!launch_page(a, pg0)) return;  // uniform over the CTA
+  int pg0 = a.pg0;
+  if (a.T_stride == 0 && !launch_page(a, 0, pg0)) return;  // one length: uniform over the CTA
   int carry = *a.cnt;
   for (int tile = 0; tile < a.n_ph; tile += 4 * kScanThreads) {
     int cnt[4];
@@ -197,9 +209,10 @@ __global__ void __launch_bounds__(kScanThreads) raw_offsets_kernel(const __grid_
       const int ph = tile + 4 * threadIdx.x + j;
       cnt[j] = 0;
       idx[j] = -1;
-      if (ph < a.n_ph) {
+      int pgj;
+      if (ph < a.n_ph && launch_page(a, a.b0 + seq_of(a, ph), pgj)) {  // sequences completing a page only
         int bi, pg, hk;
-        idx[j] = page_index(a, pg0, ph, bi, pg, hk);
+        idx[j] = page_index(a, pgj, ph, bi, pg, hk);
         cnt[j] = __popc(static_cast<uint32_t>(a.rowmask[idx[j]]) & 0xFFFFu);
       }
       local += cnt[j];
@@ -244,7 +257,7 @@ __global__ void __launch_bounds__(kEncWarps * 32) raw_copy_kernel(const __grid_c
   const int ph = blockIdx.x * kEncWarps + warp;
   if (ph >= a.n_ph) return;
   int pg0;
-  if (!launch_page(a, pg0)) return;
+  if (!launch_page(a, a.b0 + seq_of(a, ph), pg0)) return;
   int bi, pg, hk;
   const int64_t page = page_index(a, pg0, ph, bi, pg, hk);
   if (a.app_x != nullptr && pg0 + 1 < a.NP) {
@@ -377,6 +390,7 @@ extern "C" int exk_encode_pages(const uint16_t* src, int64_t s_b, int64_t s_pg, 
   a.NP = TS / kP;
   a.n_ph = static_cast<int>(n_ph);
   a.T_dev = nullptr;
+  a.T_stride = 0;
   a.app_x = nullptr;
   a.app_sb = a.app_sh = 0;
   a.tail_row0 = -1;
@@ -433,11 +447,11 @@ extern "C" int exk_decode_to_bf16(const exk_cview* c, int B, int TS, int H, int 
 
 extern "C" int exk_append_token(const uint16_t* x, int64_t x_sb, int64_t x_sh, uint8_t* sm, uint8_t* code,
                                 uint8_t* base, int32_t* rowmask, int32_t* rowoff, uint16_t* raw, int64_t raw_cap,
-                                int32_t* cnt, int B, int H, int TS, const int32_t* T_dev, int32_t* status, int device,
-                                void* stream) {
+                                int32_t* cnt, int B, int H, int TS, const int32_t* T_dev, int T_stride,
+                                int32_t* status, int device, void* stream) {
   (void)status;
   if (x == nullptr || sm == nullptr || code == nullptr || base == nullptr || rowmask == nullptr ||
-      rowoff == nullptr || raw == nullptr || cnt == nullptr || T_dev == nullptr)
+      rowoff == nullptr || raw == nullptr || cnt == nullptr || T_dev == nullptr || (T_stride != 0 && T_stride != 1))
     return EXK_EARG;
   if (B <= 0 || H <= 0 || TS <= 0 || TS % kP != 0 || raw_cap < 0) return EXK_EARG;
   if (static_cast<int64_t>(B) * H > (int64_t{1} << 30)) return EXK_EARG;
@@ -469,6 +483,7 @@ extern "C" int exk_append_token(const uint16_t* x, int64_t x_sb, int64_t x_sh, u
   a.NP = TS / kP;
   a.n_ph = B * H;
   a.T_dev = T_dev;
+  a.T_stride = T_stride;
   a.app_x = x;
   a.app_sb = x_sb;
   a.app_sh = x_sh;

@@ -238,17 +238,25 @@ def encode_pages(src, strides, buf, b0, pg0, nb, npg):
 # attention_compressed_devlen reads T from the device with the plan for the
 # caches' capacity; advance_length moves the count on. No host synchronisation.
 
+def _stride_of(T_dev, B):
+    """0: one length for the batch (a 1-element tensor); 1: one per sequence."""
+    if T_dev.dtype != torch.int32 or not T_dev.is_contiguous() or T_dev.numel() not in (1, B):
+        raise ValueError("T_dev must be a contiguous int32 tensor of 1 or B lengths")
+    return 0 if T_dev.numel() == 1 else 1
+
+
 def append_token(x, c, T_dev):
     """x [B, H, 128] bf16 (channels contiguous): the step's token for every
-    sequence of CompressedKV `c`, appended at row *T_dev."""
+    sequence of CompressedKV `c`, appended at row T_dev (one length for the
+    batch, or one per sequence)."""
     if x.dtype != torch.bfloat16 or x.stride(-1) != 1 or tuple(x.shape) != (c.B, c.H, D):
         raise ValueError("x must be bf16 [B, H, 128] with contiguous channels")
     dev = x.device
     stream = torch.cuda.current_stream(dev).cuda_stream
     rc = lib.exk_append_token(x.data_ptr(), x.stride(0), x.stride(1), c.sm.data_ptr(), c.code.data_ptr(),
                               c.base.data_ptr(), c.rowmask.data_ptr(), c.rowoff.data_ptr(), c.raw.data_ptr(), c.cap,
-                              c.cnt.data_ptr(), c.B, c.H, c.TS, T_dev.data_ptr(), status_tensor(dev.index).data_ptr(),
-                              dev.index, stream)
+                              c.cnt.data_ptr(), c.B, c.H, c.TS, T_dev.data_ptr(), _stride_of(T_dev, c.B),
+                              status_tensor(dev.index).data_ptr(), dev.index, stream)
     check(rc, "exk_append_token")
 
 
@@ -259,9 +267,10 @@ def advance_length(T_dev, n=1):
 
 
 def attention_compressed_devlen(q, kc, vc, T_dev, T_add=1, out=None, num_warps=None, advance=0):
-    """Decode attention over the first min(TS, *T_dev + T_add) tokens of the caches,
-    with the split plan for their capacity TS (see exk_attention_compressed_devlen);
-    advance != 0 then adds it to *T_dev on the device (the end of a step)."""
+    """Decode attention over the first min(TS, T_dev + T_add) tokens of the caches
+    (T_dev: one int32 length for the batch or one per sequence), with the split
+    plan for their capacity TS (see exk_attention_compressed_devlen); advance != 0
+    then adds it to the batch length on the device (the end of a step)."""
     ka, TS, Hkv = _cache_args(kc)
     va, _, _ = _cache_args(vc)
     _check_q(q, TS, TS)
@@ -272,8 +281,29 @@ def attention_compressed_devlen(q, kc, vc, T_dev, T_add=1, out=None, num_warps=N
     ws = _workspace(q.device, stream, B * Hq, ns, sl)
     out = torch.empty_like(q) if out is None else out
     rc = lib.exk_attention_compressed_devlen(q.data_ptr(), ctypes.byref(ka), ctypes.byref(va), B, TS, Hkv, Hq, TS,
-                                             T_dev.data_ptr(), T_add, advance, ctypes.byref(ws[3]), out.data_ptr(),
-                                             _consumer_warps(num_warps), D ** -0.5 * LOG2E,
-                                             status_tensor(dev).data_ptr(), dev, stream)
+                                             T_dev.data_ptr(), T_add, _stride_of(T_dev, B), advance,
+                                             ctypes.byref(ws[3]), out.data_ptr(), _consumer_warps(num_warps),
+                                             D ** -0.5 * LOG2E, status_tensor(dev).data_ptr(), dev, stream)
     check(rc, "exk_attention_compressed_devlen")
+    return out
+
+
+def attention_reference_devlen(q, k, v, T_dev, T_add=0, out=None, num_warps=None):
+    """The bf16 sibling of attention_compressed_devlen on k, v [B, TS, Hkv, 128]
+    (bit-identical for the same values, lengths and num_warps)."""
+    if k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16 or not (k.is_contiguous() and v.is_contiguous()):
+        raise ValueError("k and v must be contiguous bf16 [B, TS, Hkv, 128]")
+    TS, Hkv = k.shape[1], k.shape[2]
+    _check_q(q, TS, TS)
+    B, Hq, _ = q.shape
+    dev = q.device.index
+    stream = torch.cuda.current_stream(q.device).cuda_stream
+    ns, sl = plan_splits(B, Hkv, TS, dev)
+    ws = _workspace(q.device, stream, B * Hq, ns, sl)
+    out = torch.empty_like(q) if out is None else out
+    rc = lib.exk_attention_bf16_devlen(q.data_ptr(), k.data_ptr(), v.data_ptr(), B, TS, Hkv, Hq, TS, T_dev.data_ptr(),
+                                       T_add, _stride_of(T_dev, B), 0, ctypes.byref(ws[3]), out.data_ptr(),
+                                       _consumer_warps(num_warps), D ** -0.5 * LOG2E,
+                                       status_tensor(dev).data_ptr(), dev, stream)
+    check(rc, "exk_attention_bf16_devlen")
     return out

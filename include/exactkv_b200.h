@@ -119,18 +119,28 @@ int exk_attention_compressed(const uint16_t *q, const exk_cview *k, const exk_cv
                              uint16_t *out, int consumer_warps, float qk_scale,
                              int32_t *status, int device, void *stream);
 
-/* exk_attention_compressed with the valid length read on the device:
- * T = min(T_cap, *T_dev + T_add), so one enqueued call (e.g. inside a captured
- * CUDA graph) serves every step of a growing cache. `ws` must hold the plan for
- * T_cap (its splits exactly cover T_cap); splits past T contribute nothing.
- * Same results as exk_attention_compressed with that plan at length T. With
- * advance != 0 the merge then adds `advance` to *T_dev (the end of a step).
- * No counterpart in the reference (its calls take T on the host). */
+/* exk_attention_compressed with the valid lengths read on the device: sequence
+ * b holds T_b = min(T_cap, T_dev[b * T_stride] + T_add) tokens (T_stride 0: one
+ * length for the batch; 1: one per sequence, a variable-length batch), so one
+ * enqueued call (e.g. inside a captured CUDA graph) serves every step of a
+ * growing cache. `ws` must hold the plan for T_cap (its splits exactly cover
+ * T_cap); splits past T_b contribute nothing. Same results as
+ * exk_attention_compressed with that plan at length T_b. With advance != 0
+ * (T_stride 0 only) the merge then adds `advance` to *T_dev (the end of a
+ * step). No counterpart in the reference (its calls take one host-side T). */
 int exk_attention_compressed_devlen(const uint16_t *q, const exk_cview *k, const exk_cview *v,
                                     int B, int TS, int Hkv, int Hq, int T_cap, int32_t *T_dev,
-                                    int T_add, int advance, const exk_partials *ws, uint16_t *out,
-                                    int consumer_warps, float qk_scale, int32_t *status, int device,
-                                    void *stream);
+                                    int T_add, int T_stride, int advance, const exk_partials *ws,
+                                    uint16_t *out, int consumer_warps, float qk_scale, int32_t *status,
+                                    int device, void *stream);
+
+/* The bf16 sibling of exk_attention_compressed_devlen (bit-identical on the same
+ * values, plan, lengths and consumer_warps). */
+int exk_attention_bf16_devlen(const uint16_t *q, const uint16_t *k, const uint16_t *v,
+                              int B, int TS, int Hkv, int Hq, int T_cap, int32_t *T_dev, int T_add,
+                              int T_stride, int advance, const exk_partials *ws, uint16_t *out,
+                              int consumer_warps, float qk_scale, int32_t *status, int device,
+                              void *stream);
 
 /* The bf16 sibling of exk_attention_compressed (bit-identical on the same values,
  * plan and consumer_warps). Replaces attention_reference (exactkv/kernels.py:321-328). */
@@ -154,8 +164,9 @@ int exk_encode_pages(const uint16_t *src, int64_t s_b, int64_t s_pg, int64_t s_p
                      int32_t *status, int device, void *stream);
 
 /* One decode step's append with the length on the device (the whole step can
- * be enqueued once and replayed, e.g. in a CUDA graph). *T_dev = tokens held
- * before the step. Writes x [B, H, 128] (strides x_sb, x_sh; channels
+ * be enqueued once and replayed, e.g. in a CUDA graph). T_dev[b * T_stride] =
+ * tokens sequence b holds before the step (T_stride 0: one length for the
+ * batch; 1: a variable-length batch, each sequence on its own row and pages). Writes x [B, H, 128] (strides x_sb, x_sh; channels
  * contiguous) into row *T_dev % 16 of each (sequence, head)'s tail page — the
  * raw rows [raw_cap + (b*H + h)*16, +16) of the pool — and, when that fills
  * page (*T_dev + 1)/16 - 1, encodes the page exactly as exk_encode_pages does
@@ -167,8 +178,8 @@ int exk_encode_pages(const uint16_t *src, int64_t s_b, int64_t s_pg, int64_t s_p
  * (exactkv/cache.py:100-119) without its host synchronisation. */
 int exk_append_token(const uint16_t *x, int64_t x_sb, int64_t x_sh, uint8_t *sm, uint8_t *code,
                      uint8_t *base, int32_t *rowmask, int32_t *rowoff, uint16_t *raw, int64_t raw_cap,
-                     int32_t *cnt, int B, int H, int TS, const int32_t *T_dev, int32_t *status,
-                     int device, void *stream);
+                     int32_t *cnt, int B, int H, int TS, const int32_t *T_dev, int T_stride,
+                     int32_t *status, int device, void *stream);
 
 /* *T_dev += n on `stream` (the end of a device-length decode step). */
 int exk_advance_length(int32_t *T_dev, int n, int device, void *stream);
