@@ -101,7 +101,7 @@ __device__ __forceinline__ void load_row_quads(const uint16_t* p, int q, uint32_
 }
 
 template <bool VEC>
-__global__ void __launch_bounds__(kEncWarps * 32) encode_kernel(const __grid_constant__ EncArgs a) {
+__global__ void __launch_bounds__(kEncWarps * 32, 4) encode_kernel(const __grid_constant__ EncArgs a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ph = blockIdx.x * kEncWarps + warp;
   if (ph >= a.n_ph) return;  // whole warp
@@ -119,24 +119,26 @@ __global__ void __launch_bounds__(kEncWarps * 32) encode_kernel(const __grid_con
   int bi, pg, hk;
   const int64_t page = page_index(a, pg0, ph, bi, pg, hk);
 
-  uint32_t v[8][4];  // [token][word]: bf16 pairs (4q,4q+1), (4q+2,4q+3), (64+4q, ..), (64+4q+2, ..)
-#pragma unroll
-  for (int i = 0; i < 8; ++i)
-    load_row_quads<VEC>(a.src + bi * a.s_b + pg * a.s_pg + static_cast<int64_t>(th * 8 + i) * a.s_p + hk * a.s_h,
-                        q, v[i]);
-  // per-channel maximum exponent and zero presence over the 16 tokens
+  // Two streaming passes over the lane's 8 rows (the second re-reads them from
+  // L1): few registers, so four CTAs (32 warps) fit on an SM to hide latency.
+  // w: bf16 pairs (4q,4q+1), (4q+2,4q+3), (64+4q, ..), (64+4q+2, ..) of one row
+  const uint16_t* rows = a.src + bi * a.s_b + pg * a.s_pg + static_cast<int64_t>(th * 8) * a.s_p + hk * a.s_h;
+  // pass 1: per-channel maximum exponent and zero presence over the 16 tokens
   int emax[8];
   uint32_t has0 = 0;
 #pragma unroll
   for (int c = 0; c < 8; ++c) emax[c] = 0;
 #pragma unroll
-  for (int i = 0; i < 8; ++i)
+  for (int i = 0; i < 8; ++i) {
+    uint32_t w[4];
+    load_row_quads<VEC>(rows + static_cast<int64_t>(i) * a.s_p, q, w);
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
-      const int e = (half_of(v[i], c) >> 7) & 0xFF;
+      const int e = (half_of(w, c) >> 7) & 0xFF;
       emax[c] = max(emax[c], e);
       has0 |= (e == 0 ? 1u : 0u) << c;
     }
+  }
 #pragma unroll
   for (int c = 0; c < 8; ++c) emax[c] = max(emax[c], __shfl_xor_sync(0xFFFFFFFFu, emax[c], 16));
   has0 |= __shfl_xor_sync(0xFFFFFFFFu, has0, 16);
@@ -152,16 +154,19 @@ __global__ void __launch_bounds__(kEncWarps * 32) encode_kernel(const __grid_con
     bw[c >> 2] |= uint32_t(byte) << (8 * (c & 3));
   }
 
+  // pass 2: codes, sign|mantissa bytes and escapes, row by row
   uint32_t escrow = 0;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int tok = th * 8 + i;
     const int64_t row = (static_cast<int64_t>(a.b0 + bi) * a.TS + (pg0 + pg) * kP + tok) * a.H + hk;
+    uint32_t w[4];
+    load_row_quads<VEC>(rows + static_cast<int64_t>(i) * a.s_p, q, w);
     uint32_t smw[2] = {0u, 0u}, cw = 0u;
     bool esc = false;
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
-      const uint32_t u = half_of(v[i], c);
+      const uint32_t u = half_of(w, c);
       const int e = (u >> 7) & 0xFF;
       const bool zero = zm[c] && e == 0;
       int code = zero ? 0 : e - bse[c];
