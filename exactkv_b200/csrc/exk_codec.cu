@@ -512,3 +512,22 @@ extern "C" int exk_advance_length(int32_t* T_dev, int n, int device, void* strea
   advance_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(T_dev, n);
   return launch_status();
 }
+
+// Self-test of the bounded wait every kernel uses: one thread waits on an
+// mbarrier that nothing arrives at, gives up after limit_ns and records
+// EXK_S_FULL_TIMEOUT, exactly as a consumer whose stage never lands would.
+// No copy is in flight, so giving up is safe.
+__global__ void wait_timeout_selftest(int32_t* status, uint64_t limit_ns) {
+  __shared__ uint64_t bar;
+  mbar_init(&bar, 1);
+  fence_mbar_init();
+  if (!mbar_wait(&bar, 0u, limit_ns)) set_status(status, EXK_S_FULL_TIMEOUT);
+}
+
+extern "C" int exk_selftest_wait_timeout(int32_t* status, uint64_t limit_ns, int device, void* stream) {
+  if (status == nullptr || limit_ns == 0 || limit_ns > kWaitLimitNs) return EXK_EARG;
+  int r = use_device(device, nullptr);
+  if (r != 0) return r;
+  wait_timeout_selftest<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(status, limit_ns);
+  return launch_status();
+}

@@ -13,7 +13,7 @@ namespace exk {
 
 constexpr int kD = EXK_HEAD_DIM;  // head dimension (channels)
 constexpr int kP = EXK_PAGE;      // tokens per page
-// Bound on every spin-wait in these kernels (mbarrier, encoder chain).
+// Bound on every spin-wait in these kernels (the mbarrier waits).
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
 __device__ __forceinline__ uint64_t globaltimer() {
@@ -108,12 +108,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Waits for the phase of `bar` with parity `parity` to complete; gives up
-// after kWaitLimitNs and returns false.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// after limit_ns (the kernels use kWaitLimitNs) and returns false.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (!mbar_try_wait(bar, parity)) {
-    if (globaltimer() - t0 > kWaitLimitNs) return false;
+    if (globaltimer() - t0 > limit_ns) return false;
   }
   return true;
 }

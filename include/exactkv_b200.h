@@ -181,6 +181,13 @@ int exk_append_token(const uint16_t *x, int64_t x_sb, int64_t x_sh, uint8_t *sm,
                      int32_t *cnt, int B, int H, int TS, const int32_t *T_dev, int T_stride,
                      int32_t *status, int device, void *stream);
 
+/* Failure-detection self-test: one thread waits for an mbarrier phase that never
+ * completes, with the kernels' own bounded wait shortened to limit_ns (at most
+ * the kernels' 2 s), and writes EXK_S_FULL_TIMEOUT to *status when it gives up.
+ * Nothing is in flight, so the context stays usable. No counterpart in the
+ * reference. */
+int exk_selftest_wait_timeout(int32_t *status, uint64_t limit_ns, int device, void *stream);
+
 /* *T_dev += n on `stream` (the end of a device-length decode step). */
 int exk_advance_length(int32_t *T_dev, int n, int device, void *stream);
 

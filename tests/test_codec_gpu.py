@@ -137,3 +137,19 @@ def test_gpu_encoder_pool_overflow_counts_and_skips():
     for f in ("sm", "code", "base", "rowmask", "rowoff"):
         assert np.array_equal(getattr(c, f).cpu().numpy(), ref[f]), f
     kernels.check_status()
+
+
+def test_bounded_wait_reports_timeout():
+    """Failure detection without a fault: a wait on a barrier that nothing completes
+    gives up after its limit and reports EXK_S_FULL_TIMEOUT in the status word;
+    the context stays usable (a kernel call right after works)."""
+    import time
+    from exactkv_b200 import _lib
+    st = torch.zeros(1, dtype=torch.int32, device="cuda")
+    t0 = time.perf_counter()
+    rc = _lib.lib.exk_selftest_wait_timeout(st.data_ptr(), 5_000_000, 0, torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    assert int(st.item()) == 1                       # EXK_S_FULL_TIMEOUT
+    assert time.perf_counter() - t0 < 2.0
+    x = torch.ones(4, device="cuda")
+    assert float((x * 2).sum().item()) == 8.0
