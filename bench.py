@@ -76,6 +76,7 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-engine", action="store_true")
+    ap.add_argument("--no-kv-split", action="store_true")
     ap.add_argument("--engine-steps", type=int, default=24)
     ap.add_argument("--num-warps", type=int, default=8)
     ap.add_argument("--quick", action="store_true",
@@ -306,6 +307,10 @@ def run_ours(a, rank, world, local):
 
     encoder = None if a.quick else time_encoder(kbf, B, T, Hkv, dev)
 
+    kv_split = None
+    if not (a.no_kv_split or a.quick):
+        kv_split = run_kv_split(a, dev, rank, world)
+
     engine = None
     if not (a.no_engine or a.quick):
         del kbf, vbf
@@ -345,6 +350,7 @@ def run_ours(a, rank, world, local):
         "clocks": clocks.summary(),
         "e2e": e2e,
         "engine": engine,
+        "kv_split": kv_split,
         "cpu_baseline": cpu,
     }
     if rank == 0:
@@ -464,6 +470,62 @@ def run_e2e(a, kc, vc, B, Hq, Hkv, T0, dev, world, raw_rows0, ns0):
                     "device-length step (append + page encode at boundaries, decode attention, length advance; "
                     "pools kept ahead with one sync per 8 pages), D2H output into pinned memory; "
                     "context grows from 4096"}
+
+
+def run_kv_split(a, dev, rank, world, T=131072, Hq=32, Hkv=8, reps=20):
+    """one sequence of 131072 tokens (2% forced raw rows) split
+    over the ranks by KV sequence; per call: local split partials, NCCL all-gather
+    of the packed partials, merge in split order (exactkv_b200.parallel)."""
+    import torch
+    import torch.distributed as dist
+
+    import exactkv_b200 as ekv
+    from exactkv_b200 import parallel, synthetic
+
+    plan = parallel.KVSplitPlan.make(1, Hkv, T, world, dev)
+    t0, t1 = plan.tokens(rank)
+    n = t1 - t0
+    TS = max(16, -(-n // 16) * 16)
+    caches = []
+    for j, key in enumerate((True, False)):
+        x = synthetic.make_kv(1, T, Hkv, seed=500 + j, theta=1e6, key=key, raw_frac=0.02, device=dev)[:, t0:t1]
+        c = ekv.CompressedKV(1, TS, Hkv, 128, device=dev, reserve=0.03)
+        if n:
+            c.prefill_slot(0, x.contiguous())
+        caches.append(c)
+        del x
+    q = synthetic.make_q(1, Hq, seed=502, device=dev)
+    kc, vc = caches
+
+    def call():
+        if world > 1:
+            return parallel.attention_kv_split(q, kc, vc, plan, rank)
+        packed = parallel.local_partials(q, kc, vc, plan, 0)
+        o, m, l = parallel.assemble([packed], plan)
+        return parallel.merge(o, m, l, torch.empty_like(q))
+
+    for _ in range(3):
+        call()
+    stream = torch.cuda.current_stream(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        call()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    us = e0.elapsed_time(e1) / reps * 1e3
+    t = torch.tensor([us], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    us = float(t.item())
+    nbytes = sum(c.nbytes() for c in caches)        # this rank's compressed cache (an upper bound of what it reads)
+    return {"us_per_call": round(us, 2), "context": T, "ranks": world, "splits": plan.ns,
+            "split_len": plan.split_len, "tokens_per_rank": n, "compressed_mb_per_rank": round(nbytes / 1e6, 1),
+            "what": "1 x 131072 decode attention (32 q / 8 kv, 2% raw rows) split by KV sequence over the ranks: "
+                    "local partials + NCCL all-gather + merge in split order, max over ranks"}
 
 
 def run_engine(a, dev, world, context=4096, warm=4):
