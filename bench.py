@@ -474,8 +474,9 @@ def run_e2e(a, kc, vc, B, Hq, Hkv, T0, dev, world, raw_rows0, ns0):
 
 def run_kv_split(a, dev, rank, world, T=131072, Hq=32, Hkv=8, reps=20):
     """one sequence of 131072 tokens (2% forced raw rows) split
-    over the ranks by KV sequence; per call: local split partials, NCCL all-gather
-    of the packed partials, merge in split order (exactkv_b200.parallel)."""
+    over the ranks by KV sequence; per call: the split kernel writing the rank's
+    partial block, NCCL all-gather of the blocks, the gathered merge in split
+    order (exactkv_b200.parallel)."""
     import torch
     import torch.distributed as dist
 
@@ -500,9 +501,8 @@ def run_kv_split(a, dev, rank, world, T=131072, Hq=32, Hkv=8, reps=20):
     def call():
         if world > 1:
             return parallel.attention_kv_split(q, kc, vc, plan, rank)
-        packed = parallel.local_partials(q, kc, vc, plan, 0)
-        o, m, l = parallel.assemble([packed], plan)
-        return parallel.merge(o, m, l, torch.empty_like(q))
+        local = parallel.local_partials(q, kc, vc, plan, 0)
+        return parallel.merge_gathered(local.view(1, -1), plan, torch.empty_like(q))
 
     for _ in range(3):
         call()
@@ -525,7 +525,7 @@ def run_kv_split(a, dev, rank, world, T=131072, Hq=32, Hkv=8, reps=20):
     return {"us_per_call": round(us, 2), "context": T, "ranks": world, "splits": plan.ns,
             "split_len": plan.split_len, "tokens_per_rank": n, "compressed_mb_per_rank": round(nbytes / 1e6, 1),
             "what": "1 x 131072 decode attention (32 q / 8 kv, 2% raw rows) split by KV sequence over the ranks: "
-                    "local partials + NCCL all-gather + merge in split order, max over ranks"}
+                    "rank partial block + NCCL all_gather_into_tensor + gathered merge in split order, max over ranks"}
 
 
 def run_engine(a, dev, world, context=4096, warm=4):

@@ -541,24 +541,72 @@ __device__ __forceinline__ void load_q(const AttnArgs& a, int b, int hk, int g, 
 
 // ------------------------------------------------------------------ split merge
 
+// Partials of one workspace: o [rows, ns, 128], m, l [rows, ns].
+struct WsSplits {
+  const float* o_;
+  const float* m_;
+  const float* l_;
+  int64_t row, ns;
+  __device__ const float* m(int s) const { return m_ + row * ns + s; }
+  __device__ const float* l(int s) const { return l_ + row * ns + s; }
+  __device__ const float4* o(int s) const { return reinterpret_cast<const float4*>(o_ + (row * ns + s) * kD); }
+};
+
+constexpr int kMaxRanks = 16;
+
+// Partials gathered from `world` GPUs: rank r's block (rows * nmax * 130
+// floats, rounded up to a multiple of 4 so that every block starts 16-byte
+// aligned) holds o [rows, nmax, 128], then m, l [rows, nmax]; its first cnt[r]
+// splits are splits pre[r] .. pre[r] + cnt[r] - 1 of the whole sequence.
+struct GatherArgs {
+  const float* buf;
+  int64_t block;        // floats per rank block
+  int rows, nmax, world, ns;
+  int pre[kMaxRanks + 1];
+};
+
+struct GatheredSplits {
+  const GatherArgs* g;
+  int64_t row;
+  __device__ const float* base(int s, int& j) const {
+    int r = 0;
+    while (r + 1 < g->world && s >= g->pre[r + 1]) ++r;
+    j = s - g->pre[r];
+    return g->buf + r * g->block;
+  }
+  __device__ const float* m(int s) const {
+    int j;
+    const float* b = base(s, j);
+    return b + static_cast<int64_t>(g->rows) * g->nmax * kD + row * g->nmax + j;
+  }
+  __device__ const float* l(int s) const {
+    int j;
+    const float* b = base(s, j);
+    return b + static_cast<int64_t>(g->rows) * g->nmax * (kD + 1) + row * g->nmax + j;
+  }
+  __device__ const float4* o(int s) const {
+    int j;
+    const float* b = base(s, j);
+    return reinterpret_cast<const float4*>(b + (row * g->nmax + j) * kD);
+  }
+};
+
 // out[row] = sum_s w_s o_s / sum_s w_s l_s with w_s = 2^(m_s - max_s m_s), by
 // one warp (the reference's _reduce_kernel, exactkv/kernels.py:33-43). The
 // split weights come from all (m, l) pairs at once (lane s holds split s, 32
 // splits per round); the o rows are summed in split order with their loads
-// batched 8 at a time.
-__device__ __forceinline__ void merge_row(const float* __restrict__ o, const float* __restrict__ m,
-                                          const float* __restrict__ l, int ns, int64_t row, int lane,
-                                          uint16_t* __restrict__ out) {
-  const float* mr = m + row * ns;
-  const float* lr = l + row * ns;
-  const float4* orow = reinterpret_cast<const float4*>(o + row * ns * kD) + lane;
+// batched 8 at a time. `loc` gives the addresses of split s of the row (m, l
+// and the lane's float4 of o), so partials laid out by one workspace or
+// gathered from several GPUs merge with the same arithmetic, bit for bit.
+template <class Loc>
+__device__ __forceinline__ void merge_row(const Loc& loc, int ns, int lane, uint16_t* __restrict__ out_row) {
   if (ns <= 16) {
     // every load at once (one round trip), then the same sums in the same order
-    const float mv = lane < ns ? __ldcg(mr + lane) : -INFINITY;
-    const float lv = lane < ns ? __ldcg(lr + lane) : 0.f;
+    const float mv = lane < ns ? __ldcg(loc.m(lane)) : -INFINITY;
+    const float lv = lane < ns ? __ldcg(loc.l(lane)) : 0.f;
     float4 v[16];
 #pragma unroll
-    for (int u = 0; u < 16; ++u) v[u] = u < ns ? __ldcg(orow + u * (kD / 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int u = 0; u < 16; ++u) v[u] = u < ns ? __ldcg(loc.o(u) + lane) : make_float4(0.f, 0.f, 0.f, 0.f);
     float M = mv;
 #pragma unroll
     for (int d = 16; d > 0; d >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, d));
@@ -580,19 +628,19 @@ __device__ __forceinline__ void merge_row(const float* __restrict__ o, const flo
     uint2 r;
     r.x = pack_bf16x2(acc.x / den, acc.y / den);
     r.y = pack_bf16x2(acc.z / den, acc.w / den);
-    reinterpret_cast<uint2*>(out + row * kD)[lane] = r;
+    reinterpret_cast<uint2*>(out_row)[lane] = r;
     return;
   }
   float M = -INFINITY;
-  for (int s0 = 0; s0 < ns; s0 += 32) M = fmaxf(M, s0 + lane < ns ? __ldcg(mr + s0 + lane) : -INFINITY);
+  for (int s0 = 0; s0 < ns; s0 += 32) M = fmaxf(M, s0 + lane < ns ? __ldcg(loc.m(s0 + lane)) : -INFINITY);
 #pragma unroll
   for (int d = 16; d > 0; d >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, d));
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   float den = 0.f;
   for (int s0 = 0; s0 < ns; s0 += 32) {
     const int n = min(32, ns - s0);
-    const float w = lane < n ? ex2(__ldcg(mr + s0 + lane) - M) : 0.f;
-    float lw = lane < n ? w * __ldcg(lr + s0 + lane) : 0.f;
+    const float w = lane < n ? ex2(__ldcg(loc.m(s0 + lane)) - M) : 0.f;
+    float lw = lane < n ? w * __ldcg(loc.l(s0 + lane)) : 0.f;
 #pragma unroll
     for (int d = 16; d > 0; d >>= 1) lw += __shfl_xor_sync(0xFFFFFFFFu, lw, d);
     den += lw;
@@ -600,7 +648,7 @@ __device__ __forceinline__ void merge_row(const float* __restrict__ o, const flo
     for (; j + 8 <= n; j += 8) {
       float4 v[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) v[u] = __ldcg(orow + static_cast<int64_t>(s0 + j + u) * (kD / 4));
+      for (int u = 0; u < 8; ++u) v[u] = __ldcg(loc.o(s0 + j + u) + lane);
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
         const float wu = __shfl_sync(0xFFFFFFFFu, w, j + u);
@@ -611,7 +659,7 @@ __device__ __forceinline__ void merge_row(const float* __restrict__ o, const flo
       }
     }
     for (; j < n; ++j) {
-      const float4 v = __ldcg(orow + static_cast<int64_t>(s0 + j) * (kD / 4));
+      const float4 v = __ldcg(loc.o(s0 + j) + lane);
       const float wu = __shfl_sync(0xFFFFFFFFu, w, j);
       acc.x += wu * v.x;
       acc.y += wu * v.y;
@@ -622,7 +670,83 @@ __device__ __forceinline__ void merge_row(const float* __restrict__ o, const flo
   uint2 r;
   r.x = pack_bf16x2(acc.x / den, acc.y / den);
   r.y = pack_bf16x2(acc.z / den, acc.w / den);
-  reinterpret_cast<uint2*>(out + row * kD)[lane] = r;
+  reinterpret_cast<uint2*>(out_row)[lane] = r;
+}
+
+// Splits above which a row is merged by a whole CTA instead of one warp.
+constexpr int kWideSplits = 32;
+constexpr int kWideWarps = 8;
+
+// merge_row for many splits (ns > kWideSplits), by all kWideWarps warps of the
+// CTA: the maximum over every split first; then warp w sums its contiguous
+// chunk of splits in order (as merge_row does), and warp 0 adds the warps'
+// sums in warp order. The order depends only on ns, so every caller with the
+// same splits gets the same bits.
+template <class Loc>
+__device__ __forceinline__ void merge_row_wide(const Loc& loc, int ns, uint16_t* __restrict__ out_row) {
+  __shared__ float s_max[kWideWarps], s_den[kWideWarps];
+  __shared__ float4 s_acc[kWideWarps][32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float M = -INFINITY;
+  for (int s = threadIdx.x; s < ns; s += kWideWarps * 32) M = fmaxf(M, __ldcg(loc.m(s)));
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, d));
+  if (lane == 0) s_max[warp] = M;
+  __syncthreads();
+#pragma unroll
+  for (int w = 0; w < kWideWarps; ++w) M = fmaxf(M, s_max[w]);
+  const int c0 = warp * ns / kWideWarps, c1 = (warp + 1) * ns / kWideWarps;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float den = 0.f;
+  for (int s0 = c0; s0 < c1; s0 += 32) {
+    const int n = min(32, c1 - s0);
+    const float w = lane < n ? ex2(__ldcg(loc.m(s0 + lane)) - M) : 0.f;
+    float lw = lane < n ? w * __ldcg(loc.l(s0 + lane)) : 0.f;
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) lw += __shfl_xor_sync(0xFFFFFFFFu, lw, d);
+    den += lw;
+    int j = 0;
+    for (; j + 8 <= n; j += 8) {
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = __ldcg(loc.o(s0 + j + u) + lane);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float wu = __shfl_sync(0xFFFFFFFFu, w, j + u);
+        acc.x += wu * v[u].x;
+        acc.y += wu * v[u].y;
+        acc.z += wu * v[u].z;
+        acc.w += wu * v[u].w;
+      }
+    }
+    for (; j < n; ++j) {
+      const float4 v = __ldcg(loc.o(s0 + j) + lane);
+      const float wu = __shfl_sync(0xFFFFFFFFu, w, j);
+      acc.x += wu * v.x;
+      acc.y += wu * v.y;
+      acc.z += wu * v.z;
+      acc.w += wu * v.w;
+    }
+  }
+  s_acc[warp][lane] = acc;
+  if (lane == 0) s_den[warp] = den;
+  __syncthreads();
+  if (warp != 0) return;
+  acc = s_acc[0][lane];
+  den = s_den[0];
+#pragma unroll
+  for (int w = 1; w < kWideWarps; ++w) {
+    const float4 t = s_acc[w][lane];
+    acc.x += t.x;
+    acc.y += t.y;
+    acc.z += t.z;
+    acc.w += t.w;
+    den += s_den[w];
+  }
+  uint2 r;
+  r.x = pack_bf16x2(acc.x / den, acc.y / den);
+  r.y = pack_bf16x2(acc.z / den, acc.w / den);
+  reinterpret_cast<uint2*>(out_row)[lane] = r;
 }
 
 // ------------------------------------------------------------------ kernel
@@ -980,18 +1104,41 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
 
 // ------------------------------------------------------------------ merge
 
-__global__ void __launch_bounds__(128) merge_kernel(const float* __restrict__ o, const float* __restrict__ m,
-                                                    const float* __restrict__ l, int ns, int rows,
-                                                    uint16_t* __restrict__ out, int32_t* advance, int n_adv) {
+// WIDE = false: four rows per 128-thread CTA, one warp each; WIDE = true
+// (ns > kWideSplits): one row per CTA of kWideWarps warps.
+template <bool WIDE>
+__global__ void __launch_bounds__(WIDE ? kWideWarps * 32 : 128)
+    merge_kernel(const float* __restrict__ o, const float* __restrict__ m, const float* __restrict__ l, int ns,
+                 int rows, uint16_t* __restrict__ out, int32_t* advance, int n_adv) {
   // Launched as a programmatic dependent of the split kernel: the CTAs may be
   // resident early; this waits until the split grid has finished and its
   // partials are visible (a no-op after an ordinary launch).
   asm volatile("griddepcontrol.wait;" ::: "memory");
   // a device-length step ends here: the split kernel has read the length
   if (advance != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *advance += n_adv;
-  const int row = blockIdx.x * 4 + (threadIdx.x >> 5);
-  if (row >= rows) return;
-  merge_row(o, m, l, ns, row, threadIdx.x & 31, out);
+  if constexpr (WIDE) {
+    const int row = blockIdx.x;
+    merge_row_wide(WsSplits{o, m, l, row, ns}, ns, out + static_cast<int64_t>(row) * kD);
+  } else {
+    const int row = blockIdx.x * 4 + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    merge_row(WsSplits{o, m, l, row, ns}, ns, threadIdx.x & 31, out + static_cast<int64_t>(row) * kD);
+  }
+}
+
+// The merge of partials all-gathered from the GPUs of a KV-sequence split, in
+// global split order (rank order, then each rank's own order).
+template <bool WIDE>
+__global__ void __launch_bounds__(WIDE ? kWideWarps * 32 : 128)
+    merge_gathered_kernel(const __grid_constant__ GatherArgs g, uint16_t* __restrict__ out) {
+  if constexpr (WIDE) {
+    const int row = blockIdx.x;
+    merge_row_wide(GatheredSplits{&g, row}, g.ns, out + static_cast<int64_t>(row) * kD);
+  } else {
+    const int row = blockIdx.x * 4 + (threadIdx.x >> 5);
+    if (row >= g.rows) return;
+    merge_row(GatheredSplits{&g, row}, g.ns, threadIdx.x & 31, out + static_cast<int64_t>(row) * kD);
+  }
 }
 
 
@@ -1209,9 +1356,10 @@ int split_bf16(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, i
 // (its CTAs are scheduled early and wait in griddepcontrol.wait).
 int launch_merge(const exk_partials* ws, int rows, uint16_t* out, cudaStream_t stream, int32_t* advance = nullptr,
                  int n_adv = 0) {
+  const bool wide = ws->ns > kWideSplits;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((rows + 3) / 4);
-  cfg.blockDim = dim3(128);
+  cfg.gridDim = dim3(wide ? rows : (rows + 3) / 4);
+  cfg.blockDim = dim3(wide ? kWideWarps * 32 : 128);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -1219,7 +1367,8 @@ int launch_merge(const exk_partials* ws, int rows, uint16_t* out, cudaStream_t s
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, merge_kernel, static_cast<const float*>(ws->o),
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, wide ? merge_kernel<true> : merge_kernel<false>,
+                                           static_cast<const float*>(ws->o),
                                            static_cast<const float*>(ws->m), static_cast<const float*>(ws->l), ws->ns,
                                            rows, out, advance, n_adv);
   return e == cudaSuccess ? 0 : static_cast<int>(e);
@@ -1302,4 +1451,33 @@ extern "C" int exk_attn_merge(const exk_partials* ws, int rows, uint16_t* out, i
   int r = use_device(device, nullptr);
   if (r != 0) return r;
   return launch_merge(ws, rows, out, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int exk_attn_merge_gathered(const float* buf, int world, const int32_t* counts, int nmax, int rows,
+                                       uint16_t* out, int device, void* stream) {
+  if (buf == nullptr || counts == nullptr || out == nullptr || world <= 0 || world > kMaxRanks || nmax <= 0 ||
+      rows <= 0)
+    return EXK_EARG;
+  if (!aligned16(buf) || (reinterpret_cast<uintptr_t>(out) & 7u) != 0) return EXK_EALIGN;
+  GatherArgs g;
+  g.buf = buf;
+  g.block = (static_cast<int64_t>(rows) * nmax * (kD + 2) + 3) & ~int64_t{3};
+  g.rows = rows;
+  g.nmax = nmax;
+  g.world = world;
+  g.pre[0] = 0;
+  for (int r = 0; r < world; ++r) {
+    if (counts[r] < 0 || counts[r] > nmax) return EXK_EARG;
+    g.pre[r + 1] = g.pre[r] + counts[r];
+  }
+  for (int r = world + 1; r <= kMaxRanks; ++r) g.pre[r] = g.pre[world];
+  g.ns = g.pre[world];
+  if (g.ns <= 0) return EXK_EARG;
+  int r = use_device(device, nullptr);
+  if (r != 0) return r;
+  if (g.ns > kWideSplits)
+    merge_gathered_kernel<true><<<rows, kWideWarps * 32, 0, static_cast<cudaStream_t>(stream)>>>(g, out);
+  else
+    merge_gathered_kernel<false><<<(rows + 3) / 4, 128, 0, static_cast<cudaStream_t>(stream)>>>(g, out);
+  return launch_status();
 }

@@ -6,21 +6,41 @@ runs its own batch slice (one replica per GPU, no collective).
 KV-sequence split (one long sequence over N GPUs). A global split plan
 (ns splits of split_len tokens, chosen for N x SMs persistent CTAs) is cut
 into N contiguous runs of whole splits; rank r keeps the pages of its run,
-tokens [s0 * split_len, min(s1 * split_len, T)), in its own cache. Each rank
-computes the (o, m, l) partials of its splits with the split kernel, one
-all-gather (NCCL over NVLink) exchanges them, and every rank merges all ns
-partials in global split order. Partials depend only on their split's tokens,
-so the result is bit-identical to a single GPU running the same plan.
+tokens [s0 * split_len, min(s1 * split_len, T)), in its own cache. Each rank's
+split kernel writes the (o, m, l) partials of its splits straight into one
+flat block, one all-gather (NCCL over NVLink) exchanges the blocks, and the
+gathered-merge kernel merges all ns partials in global split order from the
+gathered buffer. Partials depend only on their split's tokens, so the result
+is bit-identical to a single GPU running the same plan.
+
+Rank block layout (fp32, `block_floats(rows, nmax)` floats, nmax = the longest
+run of splits): o [rows, nmax, 128], then m [rows, nmax], then l [rows, nmax],
+padded to a multiple of 4 floats; rank r's first counts[r] columns are valid.
 
 The reference has no multi-GPU path; the partials and the merge are those of
 its split-K decode (exactkv/kernels.py:33-43, 142-165).
 """
+import ctypes
+
 import torch
 
 from . import kernels
+from ._lib import Partials, check, lib
 from .kernels import D, P
 
-PACK = D + 2  # per (row, split): o[0:D], m, l
+MAX_RANKS = 16  # ranks the gathered merge takes
+
+
+def block_floats(rows, nmax):
+    """Floats of one rank's block (o, m, l padded to 16 bytes)."""
+    return (rows * nmax * (D + 2) + 3) // 4 * 4
+
+
+def block_views(flat, rows, nmax):
+    """(o [rows, nmax, D], m [rows, nmax], l [rows, nmax]) views of one rank block."""
+    n = rows * nmax
+    return flat[: n * D].view(rows, nmax, D), flat[n * D: n * (D + 1)].view(rows, nmax), \
+        flat[n * (D + 1): n * (D + 2)].view(rows, nmax)
 
 
 class KVSplitPlan:
@@ -49,68 +69,111 @@ class KVSplitPlan:
         s0, s1 = self.splits(rank)
         return min(s0 * self.split_len, self.T), min(s1 * self.split_len, self.T)
 
+    def count(self, rank):
+        """Splits of rank `rank` that hold tokens (the valid columns of its block)."""
+        t0, t1 = self.tokens(rank)
+        return -(-(t1 - t0) // self.split_len) if t1 > t0 else 0
+
+    @property
+    def counts(self):
+        return [self.count(r) for r in range(self.world)]
+
     @property
     def max_local(self):
-        return max(self.bounds[r + 1] - self.bounds[r] for r in range(self.world))
+        return max(1, max(self.bounds[r + 1] - self.bounds[r] for r in range(self.world)))
 
 
-def local_partials(q, kc, vc, plan, rank, num_warps=None):
-    """Rank `rank`'s partials, packed [B*Hq, max_local, D+2] fp32 (columns past the
-    rank's own splits are padding). kc, vc hold the rank's tokens from position 0."""
-    B, Hq, _ = q.shape
-    rows = B * Hq
-    s0, s1 = plan.splits(rank)
-    t0, t1 = plan.tokens(rank)
-    packed = torch.zeros(rows, plan.max_local, PACK, dtype=torch.float32, device=q.device)
-    nloc = s1 - s0
-    if nloc > 0 and t1 > t0:
-        nloc = -(-(t1 - t0) // plan.split_len)  # splits that hold tokens
-        stream = torch.cuda.current_stream(q.device).cuda_stream
-        ws = kernels._workspace(q.device, stream, rows, nloc, plan.split_len)
-        kernels.attention_split(q, kc, vc, t1 - t0, ws, 0, nloc, num_warps=num_warps)
-        packed[:, :nloc, :D] = ws[0]
-        packed[:, :nloc, D] = ws[1]
-        packed[:, :nloc, D + 1] = ws[2]
-    return packed
+_BUF = {}  # (device, stream, rows, nmax, world) -> (local block, gathered blocks, Partials)
 
 
-def assemble(gathered, plan):
-    """Per-rank packed partials (a list in rank order) -> (o [rows, ns, D], m, l
-    [rows, ns]) in global split order."""
-    cols = []
-    for r, g in enumerate(gathered):
-        s0, s1 = plan.splits(r)
-        t0, t1 = plan.tokens(r)
-        n = -(-(t1 - t0) // plan.split_len) if t1 > t0 else 0
-        if n:
-            cols.append(g[:, :n])
-    full = torch.cat(cols, dim=1)
-    if full.shape[1] != -(-plan.T // plan.split_len):
-        raise RuntimeError("gathered partials do not cover the sequence")
-    return full[..., :D].contiguous(), full[..., D].contiguous(), full[..., D + 1].contiguous()
-
-
-def merge(o, m, l, out):
-    """Merge in split order with the split merge kernel; out: bf16 [B, Hq, D]."""
-    rows, ns, _ = o.shape
-    ws = (o, m, l, kernels.Partials(o.data_ptr(), m.data_ptr(), l.data_ptr(), ns, 0))
-    return kernels.merge_partials(ws, rows, out)
-
-
-def all_gather_packed(packed, group=None):
-    """All-gather of equal-shaped packed partials; returns the list in rank order."""
-    import torch.distributed as dist
-
-    world = dist.get_world_size(group)
-    bufs = [torch.empty_like(packed) for _ in range(world)]
-    dist.all_gather(bufs, packed, group=group)
+def _buffers(device, stream, rows, plan):
+    nmax = plan.max_local
+    key = (device.index, stream, rows, nmax, plan.world)
+    bufs = _BUF.get(key)
+    if bufs is None:
+        n = block_floats(rows, nmax)
+        gathered = torch.empty(plan.world, n, dtype=torch.float32, device=device)
+        local = torch.empty(n, dtype=torch.float32, device=device)
+        o, m, l = block_views(local, rows, nmax)
+        bufs = _BUF[key] = (local, gathered, Partials(o.data_ptr(), m.data_ptr(), l.data_ptr(), nmax, 0))
+    bufs[2].split_len = plan.split_len
     return bufs
 
 
-def attention_kv_split(q, kc, vc, plan, rank, group=None, num_warps=None):
-    """One decode-attention call over a sequence split across the ranks of `group`.
+def local_partials(q, kc, vc, plan, rank, num_warps=None):
+    """Rank `rank`'s partials as one flat block (columns past plan.count(rank) are
+    left unwritten). kc, vc hold the rank's tokens from position 0. The block is
+    a buffer reused by the next call on the same stream and shapes."""
+    rows = q.shape[0] * q.shape[1]
+    stream = torch.cuda.current_stream(q.device).cuda_stream
+    local, _, part = _buffers(q.device, stream, rows, plan)
+    n = plan.count(rank)
+    if n:
+        t0, t1 = plan.tokens(rank)
+        o, m, l = block_views(local, rows, plan.max_local)
+        kernels.attention_split(q, kc, vc, t1 - t0, (o, m, l, part), 0, n, num_warps=num_warps)
+    return local
+
+
+def all_gather_blocks(local, world, group=None, out=None):
+    """All-gather of the ranks' flat blocks into [world, block] (rank order):
+    one all_gather_into_tensor on NCCL, the list form elsewhere (gloo)."""
+    import torch.distributed as dist
+
+    if out is None:
+        out = torch.empty(world, local.numel(), dtype=local.dtype, device=local.device)
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(out, local, group=group)
+    else:
+        dist.all_gather(list(out.unbind(0)), local, group=group)
+    return out
+
+
+def assemble(gathered, plan, rows):
+    """Gathered blocks [world, block] -> (o [rows, ns, D], m, l [rows, ns]) in global
+    split order (a copy; the merge kernel reads the blocks in place)."""
+    cols = [[], [], []]
+    for r in range(plan.world):
+        n = plan.count(r)
+        if n:
+            for c, x in zip(cols, block_views(gathered[r], rows, plan.max_local)):
+                c.append(x[:, :n])
+    o, m, l = (torch.cat(c, dim=1).contiguous() for c in cols)
+    if o.shape[1] != -(-plan.T // plan.split_len):
+        raise RuntimeError("gathered partials do not cover the sequence")
+    return o, m, l
+
+
+def merge_gathered(gathered, plan, out):
+    """Merge of the gathered blocks in global split order into bf16 out [B, Hq, D]
+    (exk_attn_merge_gathered, on the current stream)."""
+    if plan.world > MAX_RANKS:
+        raise ValueError(f"the gathered merge takes at most {MAX_RANKS} ranks")
+    rows = out.shape[0] * out.shape[1]
+    if gathered.shape != (plan.world, block_floats(rows, plan.max_local)):
+        raise ValueError("gathered blocks do not match the plan")
+    counts = (ctypes.c_int32 * plan.world)(*plan.counts)
+    stream = torch.cuda.current_stream(out.device).cuda_stream
+    check(lib.exk_attn_merge_gathered(gathered.data_ptr(), plan.world, counts, plan.max_local, rows,
+                                      out.data_ptr(), out.device.index, stream), "exk_attn_merge_gathered")
+    return out
+
+
+def merge(o, m, l, out):
+    """Merge of partials already in global split order; out: bf16 [B, Hq, D]."""
+    rows, ns, _ = o.shape
+    ws = (o, m, l, Partials(o.data_ptr(), m.data_ptr(), l.data_ptr(), ns, 0))
+    return kernels.merge_partials(ws, rows, out)
+
+
+def attention_kv_split(q, kc, vc, plan, rank, group=None, num_warps=None, out=None):
+    """One decode-attention call over a sequence split across the ranks of `group`:
+    the rank's split kernel, one all-gather, the gathered merge.
     q: bf16 [B, Hq, 128] (the same on every rank); kc, vc: this rank's caches.
     Returns bf16 [B, Hq, 128] on every rank."""
-    packed = local_partials(q, kc, vc, plan, rank, num_warps=num_warps)
-    o, m, l = assemble(all_gather_packed(packed, group), plan)
-    return merge(o, m, l, torch.empty_like(q))
+    rows = q.shape[0] * q.shape[1]
+    stream = torch.cuda.current_stream(q.device).cuda_stream
+    _, gathered, _ = _buffers(q.device, stream, rows, plan)
+    local = local_partials(q, kc, vc, plan, rank, num_warps=num_warps)
+    all_gather_blocks(local, plan.world, group, out=gathered)
+    return merge_gathered(gathered, plan, torch.empty_like(q) if out is None else out)

@@ -109,6 +109,18 @@ int exk_attn_split_bf16(const uint16_t *q, const uint16_t *k, const uint16_t *v,
  * Replaces _reduce_kernel (exactkv/kernels.py:33-43). */
 int exk_attn_merge(const exk_partials *ws, int rows, uint16_t *out, int device, void *stream);
 
+/* Merge of split partials all-gathered from the `world` GPUs of a KV-sequence
+ * split (world <= 16), straight from the gathered buffer: rank r's block (rows
+ * * nmax * 130 floats rounded up to a multiple of 4, so each block starts
+ * 16-byte aligned) holds o [rows, nmax, 128], then m and l [rows, nmax];
+ * its first counts[r] (host array) columns are the next splits of the
+ * sequence. Same arithmetic as exk_attn_merge over the splits in order, so a
+ * split sequence gives the single-GPU result bit for bit. The reference has no
+ * multi-GPU path; the merge itself replaces _reduce_kernel
+ * (exactkv/kernels.py:33-43). */
+int exk_attn_merge_gathered(const float *buf, int world, const int32_t *counts, int nmax, int rows,
+                            uint16_t *out, int device, void *stream);
+
 /* One whole decode-attention call: every split of the plan in `ws`, then the
  * merge into bf16 out [B, Hq, 128] (exk_attn_merge), enqueued together; the
  * merge is a programmatic dependent launch, so its start overlaps the split

@@ -1,7 +1,7 @@
 """KV-sequence split over ranks (exactkv_b200.parallel).
 
 CPU (gloo, world size 2 and 3): each rank computes its splits' partials with the
-oracle, the packed partials go through the real all-gather and assemble code,
+oracle, the flat partial blocks go through the real all-gather and assemble code,
 and the merge of the gathered partials must equal the single-process oracle
 bit for bit (partials depend only on their split's tokens).
 GPU: ranks emulated one after another on one GPU (every rank's cache holds only
@@ -18,7 +18,7 @@ import torch
 import torch.multiprocessing as mp
 
 from exactkv_b200 import parallel
-from exactkv_b200.parallel import KVSplitPlan, PACK
+from exactkv_b200.parallel import KVSplitPlan, block_floats, block_views
 from oracle import attention as oatt
 from oracle.bf16 import f32_to_bits
 from oracle.synth import synth_kv, synth_q
@@ -46,18 +46,20 @@ def test_plan_partition_covers_every_split_once():
         KVSplitPlan(1, 8, 4096, 2, 4, 464)     # splits do not cover T
 
 
-def _oracle_packed(qb, kb, vb, plan, rank):
-    """Packed partials of one rank, computed by the oracle over the rank's tokens only."""
+def _oracle_block(qb, kb, vb, plan, rank):
+    """One rank's flat block of partials, computed by the oracle over the rank's tokens only."""
     t0, t1 = plan.tokens(rank)
     B, Hq, _ = qb.shape
-    packed = torch.zeros(B * Hq, plan.max_local, PACK, dtype=torch.float32)
-    if t1 > t0:
-        n = -(-(t1 - t0) // plan.split_len)
+    rows = B * Hq
+    flat = torch.zeros(block_floats(rows, plan.max_local), dtype=torch.float32)
+    n = plan.count(rank)
+    if n:
         o, m, l = oatt.split_partials(qb, kb[:, t0:t1], vb[:, t0:t1], t1 - t0, splits=(n, plan.split_len))
-        packed[:, :n, :D] = torch.from_numpy(o.reshape(B * Hq, n, D))
-        packed[:, :n, D] = torch.from_numpy(m.reshape(B * Hq, n))
-        packed[:, :n, D + 1] = torch.from_numpy(l.reshape(B * Hq, n))
-    return packed
+        bo, bm, bl = block_views(flat, rows, plan.max_local)
+        bo[:, :n] = torch.from_numpy(o.reshape(rows, n, D))
+        bm[:, :n] = torch.from_numpy(m.reshape(rows, n))
+        bl[:, :n] = torch.from_numpy(l.reshape(rows, n))
+    return flat
 
 
 def _gloo_rank(rank, world, port, args, outdir):
@@ -69,8 +71,8 @@ def _gloo_rank(rank, world, port, args, outdir):
         B, T, Hq, Hkv, ns, sl = args
         qb, kb, vb = synth_q(11, B, Hq), synth_kv(12, B, T, Hkv), synth_kv(13, B, T, Hkv, key=False)
         plan = KVSplitPlan(B, Hkv, T, world, ns, sl)
-        gathered = parallel.all_gather_packed(_oracle_packed(qb, kb, vb, plan, rank))
-        o, m, l = parallel.assemble(gathered, plan)
+        gathered = parallel.all_gather_blocks(_oracle_block(qb, kb, vb, plan, rank), world)
+        o, m, l = parallel.assemble(gathered, plan, B * Hq)
         out = oatt.merge(o.numpy(), m.numpy(), l.numpy())
         np.save(os.path.join(outdir, f"out{rank}.npy"), f32_to_bits(out).reshape(B, Hq, D))
     finally:
@@ -135,15 +137,18 @@ def test_kv_split_emulated_ranks_bit_identical(world, B, T, Hq, Hkv):
     v = synthetic.make_kv(B, T, Hkv, seed=22, key=False, device="cuda")
     q = synthetic.make_q(B, Hq, seed=23, device="cuda")
     plan = KVSplitPlan.make(B, Hkv, T, world)
-    packed = []
+    rows = B * Hq
+    gathered = torch.full((world, block_floats(rows, plan.max_local)), float("nan"), device="cuda")
     for r in range(world):
         kc, vc = _rank_caches(k, v, plan, r)
-        packed.append(parallel.local_partials(q, kc, vc, plan, r))
-    o, m, l = parallel.assemble(packed, plan)
-    out = parallel.merge(o, m, l, torch.empty_like(q))
+        gathered[r] = parallel.local_partials(q, kc, vc, plan, r)
+    out = parallel.merge_gathered(gathered, plan, torch.empty_like(q))
+    o, m, l = parallel.assemble(gathered, plan, rows)
+    out2 = parallel.merge(o, m, l, torch.empty_like(q))
     ref = _full_run(q, k, v, T, plan.ns, plan.split_len)
     kernels.check_status()
     assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
+    assert torch.equal(out2.view(torch.int16), ref.view(torch.int16))
 
 
 def _nccl_rank(rank, world, port, outdir):
