@@ -475,13 +475,14 @@ def run_e2e(a, kc, vc, B, Hq, Hkv, T0, dev, world, raw_rows0, ns0):
 def run_kv_split(a, dev, rank, world, T=131072, Hq=32, Hkv=8, reps=20):
     """one sequence of 131072 tokens (2% forced raw rows) split
     over the ranks by KV sequence; per call: the split kernel writing the rank's
-    partial block, NCCL all-gather of the blocks, the gathered merge in split
-    order (exactkv_b200.parallel)."""
+    partial block into symmetric memory, then the peer merge reading every
+    rank's block over NVLink (exactkv_b200.parallel.PeerExchange); the NCCL
+    all-gather variant is timed beside it."""
     import torch
     import torch.distributed as dist
 
     import exactkv_b200 as ekv
-    from exactkv_b200 import parallel, synthetic
+    from exactkv_b200 import kernels, parallel, synthetic
 
     plan = parallel.KVSplitPlan.make(1, Hkv, T, world, dev)
     t0, t1 = plan.tokens(rank)
@@ -498,34 +499,72 @@ def run_kv_split(a, dev, rank, world, T=131072, Hq=32, Hkv=8, reps=20):
     q = synthetic.make_q(1, Hq, seed=502, device=dev)
     kc, vc = caches
 
-    def call():
-        if world > 1:
-            return parallel.attention_kv_split(q, kc, vc, plan, rank)
-        local = parallel.local_partials(q, kc, vc, plan, 0)
-        return parallel.merge_gathered(local.view(1, -1), plan, torch.empty_like(q))
+    out = torch.empty_like(q)
+    ex = parallel.PeerExchange(plan, Hq) if world > 1 else None
 
-    for _ in range(3):
-        call()
+    def call_peer():
+        if ex is not None:
+            return ex.attention(q, kc, vc, out)
+        local = parallel.local_partials(q, kc, vc, plan, 0)
+        return parallel.merge_gathered(local.view(1, -1), plan, out)
+
+    def call_nccl():
+        return parallel.attention_kv_split(q, kc, vc, plan, rank, out=out)
+
     stream = torch.cuda.current_stream(dev)
+
+    def timed(call):
+        for _ in range(3):
+            call()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            call()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        t = torch.tensor([e0.elapsed_time(e1) / reps * 1e3], device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    us = timed(call_peer)
+    us_nccl = timed(call_nccl) if world > 1 else None
+
+    # the peer path again with an event between the split kernel and the merge
+    # (which includes the wait for the peers): this rank's average per phase
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(reps)]
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(reps):
-        call()
-    e1.record(stream)
+    for e in ev:
+        e[0].record(stream)
+        if ex is not None:
+            ex.split(q, kc, vc)
+            e[1].record(stream)
+            ex.merge(out)
+        else:
+            local = parallel.local_partials(q, kc, vc, plan, 0)
+            e[1].record(stream)
+            parallel.merge_gathered(local.view(1, -1), plan, out)
+        e[2].record(stream)
     torch.cuda.synchronize(dev)
-    us = e0.elapsed_time(e1) / reps * 1e3
-    t = torch.tensor([us], device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    us = float(t.item())
+    phases = {name: round(sum(e[i].elapsed_time(e[i + 1]) for e in ev) / reps * 1e3, 2)
+              for i, name in enumerate(("split", "merge"))}
+    if ex is not None:
+        dist.barrier()
+        ex.close()
+    kernels.check_status(dev)
     nbytes = sum(c.nbytes() for c in caches)        # this rank's compressed cache (an upper bound of what it reads)
-    return {"us_per_call": round(us, 2), "context": T, "ranks": world, "splits": plan.ns,
+    return {"us_per_call": round(us, 2), "nccl_all_gather_us_per_call": None if us_nccl is None else round(us_nccl, 2),
+            "phases_us_rank0": phases, "context": T, "ranks": world, "splits": plan.ns,
             "split_len": plan.split_len, "tokens_per_rank": n, "compressed_mb_per_rank": round(nbytes / 1e6, 1),
             "what": "1 x 131072 decode attention (32 q / 8 kv, 2% raw rows) split by KV sequence over the ranks: "
-                    "rank partial block + NCCL all_gather_into_tensor + gathered merge in split order, max over ranks"}
+                    "split kernel into the rank's symmetric-memory block, then the peer merge reading every rank's "
+                    "block over NVLink in split order (max over ranks); nccl_all_gather_us_per_call: the same with "
+                    "NCCL all_gather_into_tensor and the gathered merge"}
 
 
 def run_engine(a, dev, world, context=4096, warm=4):

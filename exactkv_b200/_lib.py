@@ -11,6 +11,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libexactkv_b200.so")
 
 c_void_p, c_int, c_int32, c_int64, c_float = ctypes.c_void_p, ctypes.c_int, ctypes.c_int32, ctypes.c_int64, ctypes.c_float
+c_uint32 = ctypes.c_uint32
 
 # Every symbol the header declares, with its ctypes signature (restype, argtypes).
 _SIGNATURES = {}
@@ -37,6 +38,8 @@ _SIGNATURES.update({
                                     _P(Partials), c_int, c_float, c_void_p, c_int, c_void_p]),
     "exk_attn_merge": (c_int, [_P(Partials), c_int, c_void_p, c_int, c_void_p]),
     "exk_attn_merge_gathered": (c_int, [c_void_p, c_int, _P(c_int32), c_int, c_int, c_void_p, c_int, c_void_p]),
+    "exk_attn_merge_peers": (c_int, [_P(c_void_p), c_int, c_int, _P(c_int32), c_int, c_int, c_void_p, _P(c_void_p),
+                                     c_uint32, c_void_p, c_void_p, c_int, c_void_p]),
     "exk_attention_compressed": (c_int, [c_void_p, _P(CView), _P(CView), c_int, c_int, c_int, c_int, c_int,
                                          _P(Partials), c_void_p, c_int, c_float, c_void_p, c_int, c_void_p]),
     "exk_attention_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, _P(Partials),

@@ -554,15 +554,22 @@ struct WsSplits {
 
 constexpr int kMaxRanks = 16;
 
-// Partials gathered from `world` GPUs: rank r's block (rows * nmax * 130
-// floats, rounded up to a multiple of 4 so that every block starts 16-byte
-// aligned) holds o [rows, nmax, 128], then m, l [rows, nmax]; its first cnt[r]
-// splits are splits pre[r] .. pre[r] + cnt[r] - 1 of the whole sequence.
+// Partials of the `world` GPUs of a KV-sequence split: rank r's block (at
+// base[r]: rows * nmax * 130 floats, rounded up to a multiple of 4) holds
+// o [rows, nmax, 128], then m, l [rows, nmax]; its first cnt[r] splits are
+// splits pre[r] .. pre[r] + cnt[r] - 1 of the whole sequence. The blocks are
+// either in this GPU's memory (all-gathered) or read in place from the peers
+// over NVLink; then `flags` is set and the merge first waits for the peers'
+// signals (peers_ready).
 struct GatherArgs {
-  const float* buf;
-  int64_t block;        // floats per rank block
+  const float* base[kMaxRanks];
   int rows, nmax, world, ns;
   int pre[kMaxRanks + 1];
+  uint32_t* flags;                 // this GPU's flag words, one per rank (nullptr: no exchange)
+  uint32_t* peer_flag[kMaxRanks];  // word `rank` of peer p's flags
+  uint32_t epoch;                  // the call's number, the same on every rank
+  int rank;
+  int32_t* status;
 };
 
 struct GatheredSplits {
@@ -572,7 +579,7 @@ struct GatheredSplits {
     int r = 0;
     while (r + 1 < g->world && s >= g->pre[r + 1]) ++r;
     j = s - g->pre[r];
-    return g->buf + r * g->block;
+    return g->base[r];
   }
   __device__ const float* m(int s) const {
     int j;
@@ -590,6 +597,53 @@ struct GatheredSplits {
     return reinterpret_cast<const float4*>(b + (row * g->nmax + j) * kD);
   }
 };
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// The exchange of a peer merge, run by every CTA before it reads any block:
+// publish this rank's epoch to every peer (the partials were written by the
+// split kernel that ran before this kernel on the stream), then wait until
+// every peer has published it too. Every CTA publishes (the stores are
+// idempotent), so no CTA's wait depends on another CTA of this grid being
+// resident. The wait gives up after kWaitLimitNs with EXK_S_PEER_TIMEOUT.
+// A block is overwritten only two calls later (the caller alternates two
+// blocks), by which time every peer has finished reading it: a rank starts
+// call e + 2 only after its merge of call e + 1, which waited for every
+// peer's signal of call e + 1, sent after that peer's merge of call e.
+__device__ __forceinline__ bool peers_ready(const GatherArgs& g) {
+  __shared__ int s_ok;
+  if (threadIdx.x < g.world && static_cast<int>(threadIdx.x) != g.rank) {
+    __threadfence_system();
+    st_release_sys(g.peer_flag[threadIdx.x], g.epoch);
+  }
+  if (threadIdx.x == 0) {
+    int ok = g.status == nullptr || *reinterpret_cast<volatile int32_t*>(g.status) == 0;
+    for (int p = 0; ok && p < g.world; ++p) {
+      if (p == g.rank) continue;
+      if (static_cast<int32_t>(ld_acquire_sys(g.flags + p) - g.epoch) >= 0) continue;
+      const uint64_t t0 = globaltimer();
+      while (static_cast<int32_t>(ld_acquire_sys(g.flags + p) - g.epoch) < 0) {
+        if (globaltimer() - t0 > kWaitLimitNs) {
+          set_status(g.status, EXK_S_PEER_TIMEOUT);
+          ok = 0;
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+    s_ok = ok;
+  }
+  __syncthreads();
+  return s_ok != 0;
+}
 
 // out[row] = sum_s w_s o_s / sum_s w_s l_s with w_s = 2^(m_s - max_s m_s), by
 // one warp (the reference's _reduce_kernel, exactkv/kernels.py:33-43). The
@@ -675,27 +729,33 @@ __device__ __forceinline__ void merge_row(const Loc& loc, int ns, int lane, uint
 
 // Splits above which a row is merged by a whole CTA instead of one warp.
 constexpr int kWideSplits = 32;
-constexpr int kWideWarps = 8;
+constexpr int kWideMaxWarps = 32;
 
-// merge_row for many splits (ns > kWideSplits), by all kWideWarps warps of the
-// CTA: the maximum over every split first; then warp w sums its contiguous
-// chunk of splits in order (as merge_row does), and warp 0 adds the warps'
-// sums in warp order. The order depends only on ns, so every caller with the
-// same splits gets the same bits.
+// Warps of the CTA that merges one row of ns > kWideSplits splits: about
+// eight splits per warp, 8 to 32 warps.
+__host__ __device__ constexpr int wide_warps(int ns) {
+  return ns / 8 < 8 ? 8 : (ns / 8 > kWideMaxWarps ? kWideMaxWarps : ns / 8);
+}
+
+// merge_row for many splits (ns > kWideSplits), by the nw = wide_warps(ns)
+// warps of the CTA: the maximum over every split first; then warp w sums its
+// contiguous chunk of splits in order (as merge_row does), and warp 0 adds
+// the warps' sums in warp order. The order depends only on ns, so every caller
+// with the same splits gets the same bits.
 template <class Loc>
 __device__ __forceinline__ void merge_row_wide(const Loc& loc, int ns, uint16_t* __restrict__ out_row) {
-  __shared__ float s_max[kWideWarps], s_den[kWideWarps];
-  __shared__ float4 s_acc[kWideWarps][32];
+  __shared__ float s_max[kWideMaxWarps], s_den[kWideMaxWarps];
+  __shared__ float4 s_acc[kWideMaxWarps][32];
+  const int nw = wide_warps(ns);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float M = -INFINITY;
-  for (int s = threadIdx.x; s < ns; s += kWideWarps * 32) M = fmaxf(M, __ldcg(loc.m(s)));
+  for (int s = threadIdx.x; s < ns; s += nw * 32) M = fmaxf(M, __ldcg(loc.m(s)));
 #pragma unroll
   for (int d = 16; d > 0; d >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, d));
   if (lane == 0) s_max[warp] = M;
   __syncthreads();
-#pragma unroll
-  for (int w = 0; w < kWideWarps; ++w) M = fmaxf(M, s_max[w]);
-  const int c0 = warp * ns / kWideWarps, c1 = (warp + 1) * ns / kWideWarps;
+  for (int w = 0; w < nw; ++w) M = fmaxf(M, s_max[w]);
+  const int c0 = warp * ns / nw, c1 = (warp + 1) * ns / nw;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   float den = 0.f;
   for (int s0 = c0; s0 < c1; s0 += 32) {
@@ -734,8 +794,7 @@ __device__ __forceinline__ void merge_row_wide(const Loc& loc, int ns, uint16_t*
   if (warp != 0) return;
   acc = s_acc[0][lane];
   den = s_den[0];
-#pragma unroll
-  for (int w = 1; w < kWideWarps; ++w) {
+  for (int w = 1; w < nw; ++w) {
     const float4 t = s_acc[w][lane];
     acc.x += t.x;
     acc.y += t.y;
@@ -1105,9 +1164,9 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
 // ------------------------------------------------------------------ merge
 
 // WIDE = false: four rows per 128-thread CTA, one warp each; WIDE = true
-// (ns > kWideSplits): one row per CTA of kWideWarps warps.
+// (ns > kWideSplits): one row per CTA of wide_warps(ns) warps.
 template <bool WIDE>
-__global__ void __launch_bounds__(WIDE ? kWideWarps * 32 : 128)
+__global__ void __launch_bounds__(WIDE ? kWideMaxWarps * 32 : 128)
     merge_kernel(const float* __restrict__ o, const float* __restrict__ m, const float* __restrict__ l, int ns,
                  int rows, uint16_t* __restrict__ out, int32_t* advance, int n_adv) {
   // Launched as a programmatic dependent of the split kernel: the CTAs may be
@@ -1126,11 +1185,13 @@ __global__ void __launch_bounds__(WIDE ? kWideWarps * 32 : 128)
   }
 }
 
-// The merge of partials all-gathered from the GPUs of a KV-sequence split, in
-// global split order (rank order, then each rank's own order).
+// The merge of the partials of the GPUs of a KV-sequence split (all-gathered
+// into this GPU's memory, or read from the peers), in global split order (rank
+// order, then each rank's own order).
 template <bool WIDE>
-__global__ void __launch_bounds__(WIDE ? kWideWarps * 32 : 128)
+__global__ void __launch_bounds__(WIDE ? kWideMaxWarps * 32 : 128)
     merge_gathered_kernel(const __grid_constant__ GatherArgs g, uint16_t* __restrict__ out) {
+  if (g.flags != nullptr && !peers_ready(g)) return;
   if constexpr (WIDE) {
     const int row = blockIdx.x;
     merge_row_wide(GatheredSplits{&g, row}, g.ns, out + static_cast<int64_t>(row) * kD);
@@ -1359,7 +1420,7 @@ int launch_merge(const exk_partials* ws, int rows, uint16_t* out, cudaStream_t s
   const bool wide = ws->ns > kWideSplits;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(wide ? rows : (rows + 3) / 4);
-  cfg.blockDim = dim3(wide ? kWideWarps * 32 : 128);
+  cfg.blockDim = dim3(wide ? wide_warps(ws->ns) * 32 : 128);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -1453,15 +1514,11 @@ extern "C" int exk_attn_merge(const exk_partials* ws, int rows, uint16_t* out, i
   return launch_merge(ws, rows, out, static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int exk_attn_merge_gathered(const float* buf, int world, const int32_t* counts, int nmax, int rows,
-                                       uint16_t* out, int device, void* stream) {
-  if (buf == nullptr || counts == nullptr || out == nullptr || world <= 0 || world > kMaxRanks || nmax <= 0 ||
-      rows <= 0)
-    return EXK_EARG;
-  if (!aligned16(buf) || (reinterpret_cast<uintptr_t>(out) & 7u) != 0) return EXK_EALIGN;
-  GatherArgs g;
-  g.buf = buf;
-  g.block = (static_cast<int64_t>(rows) * nmax * (kD + 2) + 3) & ~int64_t{3};
+namespace {
+
+// Fills the split layout of a gathered or peer merge; 0 or an EXK_E* code.
+int gather_layout(GatherArgs& g, int world, const int32_t* counts, int nmax, int rows) {
+  if (counts == nullptr || world <= 0 || world > kMaxRanks || nmax <= 0 || rows <= 0) return EXK_EARG;
   g.rows = rows;
   g.nmax = nmax;
   g.world = world;
@@ -1472,12 +1529,57 @@ extern "C" int exk_attn_merge_gathered(const float* buf, int world, const int32_
   }
   for (int r = world + 1; r <= kMaxRanks; ++r) g.pre[r] = g.pre[world];
   g.ns = g.pre[world];
-  if (g.ns <= 0) return EXK_EARG;
+  return g.ns > 0 ? 0 : EXK_EARG;
+}
+
+int launch_gathered(const GatherArgs& g, uint16_t* out, int device, void* stream) {
   int r = use_device(device, nullptr);
   if (r != 0) return r;
   if (g.ns > kWideSplits)
-    merge_gathered_kernel<true><<<rows, kWideWarps * 32, 0, static_cast<cudaStream_t>(stream)>>>(g, out);
+    merge_gathered_kernel<true><<<g.rows, wide_warps(g.ns) * 32, 0, static_cast<cudaStream_t>(stream)>>>(g, out);
   else
-    merge_gathered_kernel<false><<<(rows + 3) / 4, 128, 0, static_cast<cudaStream_t>(stream)>>>(g, out);
+    merge_gathered_kernel<false><<<(g.rows + 3) / 4, 128, 0, static_cast<cudaStream_t>(stream)>>>(g, out);
   return launch_status();
+}
+
+}  // namespace
+
+extern "C" int exk_attn_merge_gathered(const float* buf, int world, const int32_t* counts, int nmax, int rows,
+                                       uint16_t* out, int device, void* stream) {
+  if (buf == nullptr || out == nullptr) return EXK_EARG;
+  if (!aligned16(buf) || (reinterpret_cast<uintptr_t>(out) & 7u) != 0) return EXK_EALIGN;
+  GatherArgs g = {};
+  int r = gather_layout(g, world, counts, nmax, rows);
+  if (r != 0) return r;
+  const int64_t block = (static_cast<int64_t>(rows) * nmax * (kD + 2) + 3) & ~int64_t{3};
+  for (int i = 0; i < world; ++i) g.base[i] = buf + i * block;
+  return launch_gathered(g, out, device, stream);
+}
+
+extern "C" int exk_attn_merge_peers(const float* const* blocks, int world, int rank, const int32_t* counts, int nmax,
+                                    int rows, uint32_t* flags, uint32_t* const* peer_flags, uint32_t epoch,
+                                    uint16_t* out, int32_t* status, int device, void* stream) {
+  if (blocks == nullptr || out == nullptr || rank < 0 || rank >= world) return EXK_EARG;
+  if ((reinterpret_cast<uintptr_t>(out) & 7u) != 0) return EXK_EALIGN;
+  GatherArgs g = {};
+  int r = gather_layout(g, world, counts, nmax, rows);
+  if (r != 0) return r;
+  for (int i = 0; i < world; ++i) {
+    if (blocks[i] == nullptr) return EXK_EARG;
+    if (!aligned16(blocks[i])) return EXK_EALIGN;
+    g.base[i] = blocks[i];
+  }
+  if (world > 1) {
+    if (flags == nullptr || peer_flags == nullptr || (reinterpret_cast<uintptr_t>(flags) & 3u) != 0) return EXK_EARG;
+    for (int i = 0; i < world; ++i) {
+      if (i != rank && (peer_flags[i] == nullptr || (reinterpret_cast<uintptr_t>(peer_flags[i]) & 3u) != 0))
+        return EXK_EARG;
+      g.peer_flag[i] = peer_flags[i];
+    }
+    g.flags = flags;
+  }
+  g.epoch = epoch;
+  g.rank = rank;
+  g.status = status;
+  return launch_gathered(g, out, device, stream);
 }

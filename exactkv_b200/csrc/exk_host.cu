@@ -90,6 +90,7 @@ extern "C" const char* exk_status_string(int code) {
     case EXK_S_RAW_INDEX: return "rowoff/rowmask point past the end of the raw pool";
     case EXK_S_CHAIN_TIMEOUT: return "encoder CTA waited more than 2 s for its predecessor's offset";
     case EXK_S_DRAIN_TIMEOUT: return "in-flight TMA copies did not land within 2 s";
+    case EXK_S_PEER_TIMEOUT: return "peer merge waited more than 2 s for another GPU's signal";
     default: return "unknown device status";
   }
 }

@@ -17,6 +17,12 @@ Rank block layout (fp32, `block_floats(rows, nmax)` floats, nmax = the longest
 run of splits): o [rows, nmax, 128], then m [rows, nmax], then l [rows, nmax],
 padded to a multiple of 4 floats; rank r's first counts[r] columns are valid.
 
+Two exchanges: attention_kv_split all-gathers the blocks with NCCL
+(all_gather_into_tensor) and merges the gathered copy; PeerExchange keeps each
+rank's blocks in symmetric memory and its merge kernel reads the peers' blocks
+in place over NVLink after a flag handshake (no collective call; the merge is
+the only kernel that touches another GPU).
+
 The reference has no multi-GPU path; the partials and the merge are those of
 its split-K decode (exactkv/kernels.py:33-43, 142-165).
 """
@@ -177,3 +183,102 @@ def attention_kv_split(q, kc, vc, plan, rank, group=None, num_warps=None, out=No
     local = local_partials(q, kc, vc, plan, rank, num_warps=num_warps)
     all_gather_blocks(local, plan.world, group, out=gathered)
     return merge_gathered(gathered, plan, torch.empty_like(q) if out is None else out)
+
+
+FLAG_BYTES = 256  # head of a PeerExchange buffer: uint32 flag words, one per rank
+
+
+def merge_peers(blocks, plan, rank, flags, peer_flags, epoch, out):
+    """exk_attn_merge_peers with explicit device addresses (ints): blocks[r] rank
+    r's block, flags this GPU's flag words, peer_flags[p] word `rank` of peer p's
+    flags (PeerExchange builds these from symmetric memory)."""
+    w = plan.world
+    dev = out.device.index
+    stream = torch.cuda.current_stream(out.device).cuda_stream
+    check(lib.exk_attn_merge_peers((ctypes.c_void_p * w)(*blocks), w, rank, (ctypes.c_int32 * w)(*plan.counts),
+                                   plan.max_local, out.shape[0] * out.shape[1], flags,
+                                   (ctypes.c_void_p * w)(*peer_flags), epoch, out.data_ptr(),
+                                   kernels.status_tensor(dev).data_ptr(), dev, stream), "exk_attn_merge_peers")
+    return out
+
+
+class PeerExchange:
+    """KV-sequence split whose merge reads the peers' partial blocks in place.
+
+    One symmetric-memory buffer per rank (torch.distributed._symmetric_memory:
+    every rank maps every peer's buffer): [flags | block 0 | block 1]. Call e
+    (counted from 1 on every rank) writes this rank's partials into block e % 2
+    with the split kernel, then exk_attn_merge_peers signals the peers and
+    merges all ranks' blocks of that parity over NVLink. Every rank must make
+    the same calls in the same order. close() (or deleting the object) before
+    destroy_process_group."""
+
+    def __init__(self, plan, rows, group=None, device=None):
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+
+        if plan.world > MAX_RANKS:
+            raise ValueError(f"the peer merge takes at most {MAX_RANKS} ranks")
+        self.group = group if group is not None else dist.group.WORLD
+        self.rank, self.world = dist.get_rank(self.group), dist.get_world_size(self.group)
+        if self.world != plan.world:
+            raise ValueError("the plan's world size differs from the group's")
+        self.plan, self.rows = plan, rows
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        nb = block_floats(rows, plan.max_local)
+        head = FLAG_BYTES // 4
+        self.buf = symm_mem.empty(head + 2 * nb, dtype=torch.float32, device=self.device)
+        self.buf[:head].view(torch.int32).zero_()
+        self.handle = symm_mem.rendezvous(self.buf, self.group)
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)                     # every rank's flags are zero before any signal
+        ptrs = self.handle.buffer_ptrs
+        self._flags = ptrs[self.rank]
+        self._peer_flags = (ctypes.c_void_p * self.world)(*[ptrs[p] + 4 * self.rank for p in range(self.world)])
+        self._blocks, self._ws = [], []
+        for par in (0, 1):
+            off = FLAG_BYTES + par * nb * 4
+            self._blocks.append((ctypes.c_void_p * self.world)(*[ptrs[p] + off for p in range(self.world)]))
+            o, m, l = block_views(self.buf[head + par * nb: head + (par + 1) * nb], rows, plan.max_local)
+            self._ws.append((o, m, l, Partials(o.data_ptr(), m.data_ptr(), l.data_ptr(), plan.max_local,
+                                               plan.split_len)))
+        self._counts = (ctypes.c_int32 * self.world)(*plan.counts)
+        self.epoch = 0
+
+    def attention(self, q, kc, vc, out=None, num_warps=None):
+        """One decode-attention call: q bf16 [B, Hq, 128] (the same on every rank),
+        kc, vc this rank's caches; returns bf16 [B, Hq, 128] on every rank."""
+        self.split(q, kc, vc, num_warps=num_warps)
+        return self.merge(torch.empty_like(q) if out is None else out)
+
+    def split(self, q, kc, vc, num_warps=None):
+        """First half of a call: the next epoch; this rank's split kernel writes
+        its partials into its block of the epoch's parity."""
+        if self.handle is None:
+            raise RuntimeError("PeerExchange is closed")
+        if q.shape[0] * q.shape[1] != self.rows:
+            raise ValueError("q does not match the exchange's rows")
+        self.epoch += 1
+        n = self.plan.count(self.rank)
+        if n:
+            t0, t1 = self.plan.tokens(self.rank)
+            kernels.attention_split(q, kc, vc, t1 - t0, self._ws[self.epoch & 1], 0, n, num_warps=num_warps)
+
+    def merge(self, out):
+        """Second half: signal the peers, wait for theirs, merge every rank's block
+        of this epoch into bf16 out [B, Hq, 128]."""
+        dev = out.device.index
+        stream = torch.cuda.current_stream(out.device).cuda_stream
+        check(lib.exk_attn_merge_peers(self._blocks[self.epoch & 1], self.world, self.rank, self._counts,
+                                       self.plan.max_local, self.rows, self._flags, self._peer_flags,
+                                       self.epoch & 0xFFFFFFFF, out.data_ptr(),
+                                       kernels.status_tensor(dev).data_ptr(), dev, stream), "exk_attn_merge_peers")
+        return out
+
+    def close(self):
+        """Waits for this rank's work and releases the symmetric buffer (no peer
+        reads it afterwards once every rank has closed at the same call count)."""
+        if self.handle is not None:
+            torch.cuda.synchronize(self.device)
+            self.handle = None
+            self.buf = None

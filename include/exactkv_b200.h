@@ -52,6 +52,7 @@ extern "C" {
 #define EXK_S_RAW_INDEX      3  /* rowoff/rowmask pointed past the raw pool */
 #define EXK_S_CHAIN_TIMEOUT  4  /* (unused: the encoder no longer waits) */
 #define EXK_S_DRAIN_TIMEOUT  5  /* in-flight TMA copies did not land within 2 s */
+#define EXK_S_PEER_TIMEOUT   6  /* a peer merge waited > 2 s for another GPU's signal */
 
 /* One compressed cache (keys or values of one layer): the six buffers of the
  * format above. raw_rows is the number of rows `raw` holds; indices at or
@@ -120,6 +121,23 @@ int exk_attn_merge(const exk_partials *ws, int rows, uint16_t *out, int device, 
  * (exactkv/kernels.py:33-43). */
 int exk_attn_merge_gathered(const float *buf, int world, const int32_t *counts, int nmax, int rows,
                             uint16_t *out, int device, void *stream);
+
+/* exk_attn_merge_gathered without the all-gather: blocks[r] (host array of
+ * `world` device pointers, in this process's address space: this GPU's own
+ * block and the peers' blocks mapped over NVLink, e.g. symmetric memory) is
+ * rank r's block, read in place. `flags` (this GPU's uint32 [world], zeroed
+ * before the first call) and peer_flags[p] (word `rank` of peer p's flags)
+ * carry the exchange: every CTA first stores `epoch` into each peer's word
+ * (system-scope release), then waits until flags[p] >= epoch for every peer
+ * (acquire; at most 2 s, then EXK_S_PEER_TIMEOUT in *status and no output).
+ * epoch counts the calls from 1, the same on every rank, and the caller
+ * alternates two blocks per rank (the block of call e is rewritten at call
+ * e + 2, after every peer finished reading it). Each rank's split kernel must
+ * have written its block earlier on `stream`. No counterpart in the
+ * reference. */
+int exk_attn_merge_peers(const float *const *blocks, int world, int rank, const int32_t *counts, int nmax,
+                         int rows, uint32_t *flags, uint32_t *const *peer_flags, uint32_t epoch,
+                         uint16_t *out, int32_t *status, int device, void *stream);
 
 /* One whole decode-attention call: every split of the plan in `ws`, then the
  * merge into bf16 out [B, Hq, 128] (exk_attn_merge), enqueued together; the

@@ -6,7 +6,10 @@ and the merge of the gathered partials must equal the single-process oracle
 bit for bit (partials depend only on their split's tokens).
 GPU: ranks emulated one after another on one GPU (every rank's cache holds only
 its own pages) must be bit-identical to one kernel run over the whole cache
-with the same plan; with two or more GPUs, the same through NCCL.
+with the same plan, through the gathered merge and through the peer merge
+(flags already set, so nothing waits); the peer merge's wait on a flag that
+nothing sets gives up with its status code; with two or more GPUs, the same
+through NCCL and through symmetric-memory peer reads.
 """
 import os
 import socket
@@ -151,6 +154,61 @@ def test_kv_split_emulated_ranks_bit_identical(world, B, T, Hq, Hkv):
     assert torch.equal(out2.view(torch.int16), ref.view(torch.int16))
 
 
+@pytest.mark.gpu
+@pytest.mark.parametrize("world,B,T,Hq,Hkv", [(2, 1, 8192, 32, 8), (3, 2, 3000, 28, 4), (8, 1, 131072, 32, 8)])
+def test_peer_merge_emulated_ranks_bit_identical(world, B, T, Hq, Hkv):
+    from exactkv_b200 import kernels, synthetic
+    k = synthetic.make_kv(B, T, Hkv, seed=41, device="cuda")
+    v = synthetic.make_kv(B, T, Hkv, seed=42, key=False, device="cuda")
+    q = synthetic.make_q(B, Hq, seed=43, device="cuda")
+    plan = KVSplitPlan.make(B, Hkv, T, world)
+    blocks = []
+    for r in range(world):
+        kc, vc = _rank_caches(k, v, plan, r)
+        blocks.append(parallel.local_partials(q, kc, vc, plan, r).clone())
+    ref = _full_run(q, k, v, T, plan.ns, plan.split_len)
+    epoch = 5
+    for rank in range(world):                       # every rank's view: all peers already signalled
+        flags = torch.full((world,), epoch, dtype=torch.int32, device="cuda")
+        sink = torch.zeros(world, dtype=torch.int32, device="cuda")   # stands in for the peers' flag words
+        out = parallel.merge_peers([b.data_ptr() for b in blocks], plan, rank, flags.data_ptr(),
+                                   [sink.data_ptr() + 4 * p for p in range(world)], epoch, torch.empty_like(q))
+        kernels.check_status()
+        assert torch.equal(out.view(torch.int16), ref.view(torch.int16)), rank
+        assert all(sink[p].item() == (epoch if p != rank else 0) for p in range(world))
+
+
+@pytest.mark.gpu
+def test_peer_merge_wait_gives_up():
+    """A peer that never signals: the merge's bounded wait (2 s) ends with
+    EXK_S_PEER_TIMEOUT in the status word and the context stays usable."""
+    from exactkv_b200 import kernels, synthetic
+    B, T, Hq, Hkv, world = 1, 2048, 32, 8, 2
+    k = synthetic.make_kv(B, T, Hkv, seed=51, device="cuda")
+    v = synthetic.make_kv(B, T, Hkv, seed=52, key=False, device="cuda")
+    q = synthetic.make_q(B, Hq, seed=53, device="cuda")
+    plan = KVSplitPlan.make(B, Hkv, T, world)
+    kc, vc = _rank_caches(k, v, plan, 0)
+    block = parallel.local_partials(q, kc, vc, plan, 0).clone()
+    flags = torch.zeros(world, dtype=torch.int32, device="cuda")       # nothing will set flags[1]
+    sink = torch.zeros(world, dtype=torch.int32, device="cuda")
+    parallel.merge_peers([block.data_ptr()] * world, plan, 0, flags.data_ptr(),
+                         [sink.data_ptr() + 4 * p for p in range(world)], 1, torch.empty_like(q))
+    torch.cuda.synchronize()
+    st = kernels.status_tensor(torch.device("cuda", 0))
+    assert st.item() == 6                              # EXK_S_PEER_TIMEOUT
+    with pytest.raises(RuntimeError, match="peer merge"):
+        kernels.check_status()
+    assert st.item() == 0
+    # the context is intact: a whole merge with the flag set now runs
+    flags[1] = 1
+    out = parallel.merge_peers([block.data_ptr()] * world, plan, 0, flags.data_ptr(),
+                               [sink.data_ptr() + 4 * p for p in range(world)], 1, torch.empty_like(q))
+    torch.cuda.synchronize()
+    kernels.check_status()
+    assert torch.isfinite(out.float()).all()
+
+
 def _nccl_rank(rank, world, port, outdir):
     import torch.distributed as dist
     from exactkv_b200 import kernels, synthetic
@@ -169,6 +227,17 @@ def _nccl_rank(rank, world, port, outdir):
         ref = _full_run(q, k, v, T, plan.ns, plan.split_len)
         kernels.check_status()
         ok = torch.equal(out.view(torch.int16), ref.view(torch.int16))
+        # the peer merge over symmetric memory: several calls (both blocks of
+        # each rank in turn), each against its own single-GPU run
+        ex = parallel.PeerExchange(plan, B * Hq)
+        for i in range(5):
+            qi = synthetic.make_q(B, Hq, seed=300 + i, device="cuda")
+            got = ex.attention(qi, kc, vc)
+            want = _full_run(qi, k, v, T, plan.ns, plan.split_len)
+            kernels.check_status()
+            ok = ok and torch.equal(got.view(torch.int16), want.view(torch.int16))
+        ex.close()
+        dist.barrier()
         open(os.path.join(outdir, f"ok{rank}"), "w").write("1" if ok else "0")
     finally:
         dist.destroy_process_group()
