@@ -25,7 +25,8 @@ class CView(ctypes.Structure):
 
 class Partials(ctypes.Structure):
     """exk_partials: split-K workspace (o [rows, ns, 128], m, l [rows, ns]) and the split plan."""
-    _fields_ = [("o", c_void_p), ("m", c_void_p), ("l", c_void_p), ("ns", c_int32), ("split_len", c_int32)]
+    _fields_ = [("o", c_void_p), ("m", c_void_p), ("l", c_void_p), ("ns", c_int32), ("split_len", c_int32),
+                ("heads", c_int32)]
 
 
 _P = ctypes.POINTER

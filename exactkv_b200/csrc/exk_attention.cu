@@ -646,79 +646,35 @@ __device__ __forceinline__ bool peers_ready(const GatherArgs& g) {
 }
 
 // out[row] = sum_s w_s o_s / sum_s w_s l_s with w_s = 2^(m_s - max_s m_s), by
-// one warp (the reference's _reduce_kernel, exactkv/kernels.py:33-43). The
-// split weights come from all (m, l) pairs at once (lane s holds split s, 32
-// splits per round); the o rows are summed in split order with their loads
-// batched 8 at a time. `loc` gives the addresses of split s of the row (m, l
-// and the lane's float4 of o), so partials laid out by one workspace or
-// gathered from several GPUs merge with the same arithmetic, bit for bit.
+// one warp (the reference's _reduce_kernel, exactkv/kernels.py:33-43), for up
+// to kWideSplits = 16 splits: every load at once (one round trip; lane s holds
+// split s's m and l), then the sums in split order. `loc` gives the addresses
+// of split s of the row (m, l and the lane's float4 of o), so partials laid out
+// by one workspace or gathered from several GPUs merge with the same
+// arithmetic, bit for bit.
 template <class Loc>
 __device__ __forceinline__ void merge_row(const Loc& loc, int ns, int lane, uint16_t* __restrict__ out_row) {
-  if (ns <= 16) {
-    // every load at once (one round trip), then the same sums in the same order
-    const float mv = lane < ns ? __ldcg(loc.m(lane)) : -INFINITY;
-    const float lv = lane < ns ? __ldcg(loc.l(lane)) : 0.f;
-    float4 v[16];
+  const float mv = lane < ns ? __ldcg(loc.m(lane)) : -INFINITY;
+  const float lv = lane < ns ? __ldcg(loc.l(lane)) : 0.f;
+  float4 v[16];
 #pragma unroll
-    for (int u = 0; u < 16; ++u) v[u] = u < ns ? __ldcg(loc.o(u) + lane) : make_float4(0.f, 0.f, 0.f, 0.f);
-    float M = mv;
-#pragma unroll
-    for (int d = 16; d > 0; d >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, d));
-    const float w = lane < ns ? ex2(mv - M) : 0.f;
-    float den = lane < ns ? w * lv : 0.f;
-#pragma unroll
-    for (int d = 16; d > 0; d >>= 1) den += __shfl_xor_sync(0xFFFFFFFFu, den, d);
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-    for (int u = 0; u < 16; ++u) {
-      const float wu = __shfl_sync(0xFFFFFFFFu, w, u);
-      if (u < ns) {
-        acc.x += wu * v[u].x;
-        acc.y += wu * v[u].y;
-        acc.z += wu * v[u].z;
-        acc.w += wu * v[u].w;
-      }
-    }
-    uint2 r;
-    r.x = pack_bf16x2(acc.x / den, acc.y / den);
-    r.y = pack_bf16x2(acc.z / den, acc.w / den);
-    reinterpret_cast<uint2*>(out_row)[lane] = r;
-    return;
-  }
-  float M = -INFINITY;
-  for (int s0 = 0; s0 < ns; s0 += 32) M = fmaxf(M, s0 + lane < ns ? __ldcg(loc.m(s0 + lane)) : -INFINITY);
+  for (int u = 0; u < 16; ++u) v[u] = u < ns ? __ldcg(loc.o(u) + lane) : make_float4(0.f, 0.f, 0.f, 0.f);
+  float M = mv;
 #pragma unroll
   for (int d = 16; d > 0; d >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, d));
+  const float w = lane < ns ? ex2(mv - M) : 0.f;
+  float den = lane < ns ? w * lv : 0.f;
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) den += __shfl_xor_sync(0xFFFFFFFFu, den, d);
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  float den = 0.f;
-  for (int s0 = 0; s0 < ns; s0 += 32) {
-    const int n = min(32, ns - s0);
-    const float w = lane < n ? ex2(__ldcg(loc.m(s0 + lane)) - M) : 0.f;
-    float lw = lane < n ? w * __ldcg(loc.l(s0 + lane)) : 0.f;
 #pragma unroll
-    for (int d = 16; d > 0; d >>= 1) lw += __shfl_xor_sync(0xFFFFFFFFu, lw, d);
-    den += lw;
-    int j = 0;
-    for (; j + 8 <= n; j += 8) {
-      float4 v[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) v[u] = __ldcg(loc.o(s0 + j + u) + lane);
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const float wu = __shfl_sync(0xFFFFFFFFu, w, j + u);
-        acc.x += wu * v[u].x;
-        acc.y += wu * v[u].y;
-        acc.z += wu * v[u].z;
-        acc.w += wu * v[u].w;
-      }
-    }
-    for (; j < n; ++j) {
-      const float4 v = __ldcg(loc.o(s0 + j) + lane);
-      const float wu = __shfl_sync(0xFFFFFFFFu, w, j);
-      acc.x += wu * v.x;
-      acc.y += wu * v.y;
-      acc.z += wu * v.z;
-      acc.w += wu * v.w;
+  for (int u = 0; u < 16; ++u) {
+    const float wu = __shfl_sync(0xFFFFFFFFu, w, u);
+    if (u < ns) {
+      acc.x += wu * v[u].x;
+      acc.y += wu * v[u].y;
+      acc.z += wu * v[u].z;
+      acc.w += wu * v[u].w;
     }
   }
   uint2 r;
@@ -728,79 +684,84 @@ __device__ __forceinline__ void merge_row(const Loc& loc, int ns, int lane, uint
 }
 
 // Splits above which a row is merged by a whole CTA instead of one warp.
-constexpr int kWideSplits = 32;
+constexpr int kWideSplits = 16;
 constexpr int kWideMaxWarps = 32;
+constexpr int kChunk = 8;  // splits one warp loads at once
 
-// Warps of the CTA that merges one row of ns > kWideSplits splits: about
-// eight splits per warp, 8 to 32 warps.
+// Warps of the CTA that merges one row of ns > kWideSplits splits: one chunk
+// of kChunk splits each, 2 to 32 warps (more splits: each warp takes several).
 __host__ __device__ constexpr int wide_warps(int ns) {
-  return ns / 8 < 8 ? 8 : (ns / 8 > kWideMaxWarps ? kWideMaxWarps : ns / 8);
+  return (ns + kChunk - 1) / kChunk < 2 ? 2
+         : ((ns + kChunk - 1) / kChunk > kWideMaxWarps ? kWideMaxWarps : (ns + kChunk - 1) / kChunk);
 }
 
 // merge_row for many splits (ns > kWideSplits), by the nw = wide_warps(ns)
-// warps of the CTA: the maximum over every split first; then warp w sums its
-// contiguous chunk of splits in order (as merge_row does), and warp 0 adds
-// the warps' sums in warp order. The order depends only on ns, so every caller
-// with the same splits gets the same bits.
+// warps of the CTA in one memory round trip per chunk: warp w loads chunks w,
+// w + nw, ... of kChunk splits (m, l and the o rows together), folds each
+// into its running (max, sum of weights x l, sum of weights x o) in chunk
+// order, rescaling by 2^(old max - new max) when the max grows; warp 0 then
+// combines the warps in warp order, each scaled by 2^(its max - the row's).
+// Splits with m = -inf (past a sequence's length) weigh 0. The order depends
+// only on ns, so every caller with the same splits gets the same bits.
 template <class Loc>
 __device__ __forceinline__ void merge_row_wide(const Loc& loc, int ns, uint16_t* __restrict__ out_row) {
   __shared__ float s_max[kWideMaxWarps], s_den[kWideMaxWarps];
   __shared__ float4 s_acc[kWideMaxWarps][32];
   const int nw = wide_warps(ns);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float M = -INFINITY;
-  for (int s = threadIdx.x; s < ns; s += nw * 32) M = fmaxf(M, __ldcg(loc.m(s)));
-#pragma unroll
-  for (int d = 16; d > 0; d >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, d));
-  if (lane == 0) s_max[warp] = M;
-  __syncthreads();
-  for (int w = 0; w < nw; ++w) M = fmaxf(M, s_max[w]);
-  const int c0 = warp * ns / nw, c1 = (warp + 1) * ns / nw;
+  float mw = -INFINITY, den = 0.f;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  float den = 0.f;
-  for (int s0 = c0; s0 < c1; s0 += 32) {
-    const int n = min(32, c1 - s0);
-    const float w = lane < n ? ex2(__ldcg(loc.m(s0 + lane)) - M) : 0.f;
-    float lw = lane < n ? w * __ldcg(loc.l(s0 + lane)) : 0.f;
+  for (int c0 = warp * kChunk; c0 < ns; c0 += nw * kChunk) {
+    const int n = min(kChunk, ns - c0);
+    const float mv = lane < n ? __ldcg(loc.m(c0 + lane)) : -INFINITY;
+    const float lv = lane < n ? __ldcg(loc.l(c0 + lane)) : 0.f;
+    float4 v[kChunk];
+#pragma unroll
+    for (int u = 0; u < kChunk; ++u) v[u] = u < n ? __ldcg(loc.o(c0 + u) + lane) : make_float4(0.f, 0.f, 0.f, 0.f);
+    float cm = mv;
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xFFFFFFFFu, cm, d));
+    const float mn = fmaxf(mw, cm);
+    const float sc = mw == mn ? 1.f : ex2(mw - mn);  // mw = -inf < mn: 0
+    const float w = mv == -INFINITY ? 0.f : ex2(mv - mn);
+    float lw = w * lv;
 #pragma unroll
     for (int d = 16; d > 0; d >>= 1) lw += __shfl_xor_sync(0xFFFFFFFFu, lw, d);
-    den += lw;
-    int j = 0;
-    for (; j + 8 <= n; j += 8) {
-      float4 v[8];
+    den = den * sc + lw;
+    acc.x *= sc;
+    acc.y *= sc;
+    acc.z *= sc;
+    acc.w *= sc;
 #pragma unroll
-      for (int u = 0; u < 8; ++u) v[u] = __ldcg(loc.o(s0 + j + u) + lane);
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const float wu = __shfl_sync(0xFFFFFFFFu, w, j + u);
-        acc.x += wu * v[u].x;
-        acc.y += wu * v[u].y;
-        acc.z += wu * v[u].z;
-        acc.w += wu * v[u].w;
-      }
+    for (int u = 0; u < kChunk; ++u) {
+      const float wu = __shfl_sync(0xFFFFFFFFu, w, u);
+      acc.x += wu * v[u].x;
+      acc.y += wu * v[u].y;
+      acc.z += wu * v[u].z;
+      acc.w += wu * v[u].w;
     }
-    for (; j < n; ++j) {
-      const float4 v = __ldcg(loc.o(s0 + j) + lane);
-      const float wu = __shfl_sync(0xFFFFFFFFu, w, j);
-      acc.x += wu * v.x;
-      acc.y += wu * v.y;
-      acc.z += wu * v.z;
-      acc.w += wu * v.w;
-    }
+    mw = mn;
   }
   s_acc[warp][lane] = acc;
-  if (lane == 0) s_den[warp] = den;
+  if (lane == 0) {
+    s_max[warp] = mw;
+    s_den[warp] = den;
+  }
   __syncthreads();
   if (warp != 0) return;
-  acc = s_acc[0][lane];
-  den = s_den[0];
-  for (int w = 1; w < nw; ++w) {
-    const float4 t = s_acc[w][lane];
-    acc.x += t.x;
-    acc.y += t.y;
-    acc.z += t.z;
-    acc.w += t.w;
-    den += s_den[w];
+  float M = -INFINITY;
+  for (int i = 0; i < nw; ++i) M = fmaxf(M, s_max[i]);
+  acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  den = 0.f;
+  for (int i = 0; i < nw; ++i) {
+    const float mi = s_max[i];
+    const float f = mi == -INFINITY ? 0.f : ex2(mi - M);
+    const float4 t = s_acc[i][lane];
+    acc.x += f * t.x;
+    acc.y += f * t.y;
+    acc.z += f * t.z;
+    acc.w += f * t.w;
+    den += f * s_den[i];
   }
   uint2 r;
   r.x = pack_bf16x2(acc.x / den, acc.y / den);
@@ -1191,6 +1152,9 @@ __global__ void __launch_bounds__(WIDE ? kWideMaxWarps * 32 : 128)
 template <bool WIDE>
 __global__ void __launch_bounds__(WIDE ? kWideMaxWarps * 32 : 128)
     merge_gathered_kernel(const __grid_constant__ GatherArgs g, uint16_t* __restrict__ out) {
+  // a programmatic dependent of the kernel before it (the split kernel, whose
+  // partials must be complete before this rank signals its peers)
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   if (g.flags != nullptr && !peers_ready(g)) return;
   if constexpr (WIDE) {
     const int row = blockIdx.x;
@@ -1246,6 +1210,15 @@ int dispatch_split(const AttnArgs& a, const AttnMaps& maps, int hg, int grid, in
 // Heads per CTA actually used: the plan's head group, capped by the consumer warps.
 int cta_heads(int hkv, int nwc) { return std::min(head_group(hkv), nwc); }
 
+// KV heads per work item: the plan's (ws->heads) when it sets one, else the
+// default for Hkv; at most the consumer warps. -1 when the plan's is invalid.
+int item_heads(const exk_partials* ws, int hkv, int nwc) {
+  const int h = ws->heads;
+  if (h == 0) return cta_heads(hkv, nwc);
+  if ((h != 1 && h != 2 && h != 4 && h != 8) || hkv % h != 0) return -1;
+  return std::min(h, nwc);
+}
+
 // Validates the shapes shared by both split kernels and fills AttnArgs.
 int common_args(AttnArgs& a, const uint16_t* q, int B, int TS, int Hkv, int Hq, int T, int s0, int s1,
                 const exk_partials* ws, int nwc, float qk_scale, int32_t* status) {
@@ -1281,7 +1254,9 @@ int common_args(AttnArgs& a, const uint16_t* q, int B, int TS, int Hkv, int Hq, 
   // splits entirely past T (possible when s1 > the plan's last split) hold no work
   const int last = (T - 1) / ws->split_len;
   a.nsl = std::min(s1, last + 1) - s0;
-  a.ngroups = Hkv / cta_heads(Hkv, nwc);
+  const int hg = item_heads(ws, Hkv, nwc);
+  if (hg <= 0) return EXK_EARG;
+  a.ngroups = Hkv / hg;
   const int64_t items = static_cast<int64_t>(B) * a.ngroups * a.nsl;
   if (items > (int64_t{1} << 30)) return EXK_EARG;
   a.n_items = static_cast<int>(items);
@@ -1311,13 +1286,13 @@ int head_major_map(CUtensorMap* m, CUtensorMapDataType dt, const void* ptr, int 
 
 using namespace exk;
 
-extern "C" int exk_plan_splits(int B, int Hkv, int T, int num_ctas, int32_t* ns_out, int32_t* sl_out) {
-  if (B <= 0 || Hkv <= 0 || T <= 0 || num_ctas <= 0 || ns_out == nullptr || sl_out == nullptr) return EXK_EARG;
-  // Items are (sequence, head group of up to 8 heads, split); a CTA's 8 consumer
-  // warps take WPH = 8 / group pages of the group per stage. Cost of a
-  // candidate = (items on the busiest CTA) x (stages per item + a fixed
-  // per-item overhead of ~2 stages: Q load, pipeline refill, epilogue).
-  const int64_t hg = head_group(Hkv);
+namespace {
+
+// Best split of T tokens for items of hg KV heads (8 consumer warps, so a
+// stage holds 8 / hg pages of each head). Cost of a candidate = (items on the
+// busiest CTA) x (stages per item + a fixed per-item overhead of ~2 stages: Q
+// load, pipeline refill, epilogue); returns that cost.
+int64_t plan_for_heads(int B, int Hkv, int T, int num_ctas, int64_t hg, int32_t* ns_out, int32_t* sl_out) {
   const int64_t wph = 8 / hg;
   const int64_t npt = (T + kP - 1) / kP;
   const int64_t units = static_cast<int64_t>(B) * (Hkv / hg);
@@ -1342,6 +1317,15 @@ extern "C" int exk_plan_splits(int B, int Hkv, int T, int num_ctas, int32_t* ns_
   }
   *sl_out = static_cast<int32_t>(best_spp * kP);
   *ns_out = static_cast<int32_t>((npt + best_spp - 1) / best_spp);
+  return best_cost;
+}
+
+}  // namespace
+
+extern "C" int exk_plan_splits(int B, int Hkv, int T, int num_ctas, int32_t* ns_out, int32_t* sl_out) {
+  if (B <= 0 || Hkv <= 0 || T <= 0 || num_ctas <= 0 || ns_out == nullptr || sl_out == nullptr) return EXK_EARG;
+  // Items are (sequence, head group of up to 8 heads, split).
+  plan_for_heads(B, Hkv, T, num_ctas, head_group(Hkv), ns_out, sl_out);
   return 0;
 }
 
@@ -1359,7 +1343,7 @@ int split_compressed(const uint16_t* q, const exk_cview* k, const exk_cview* v, 
   a.T_stride = T_stride;
   int sms = 0;
   if ((r = use_device(device, &sms)) != 0) return r;
-  const int hg = cta_heads(Hkv, consumer_warps);
+  const int hg = item_heads(ws, Hkv, consumer_warps);
   const int wph = consumer_warps / hg;
   const exk_cview* cv[2] = {k, v};
   AttnMaps maps;
@@ -1399,7 +1383,7 @@ int split_bf16(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, i
   int sms = 0;
   if ((r = use_device(device, &sms)) != 0) return r;
   if (!aligned16(k) || !aligned16(v)) return EXK_EALIGN;
-  const int hg = cta_heads(Hkv, consumer_warps);
+  const int hg = item_heads(ws, Hkv, consumer_warps);
   const int wph = consumer_warps / hg;
   AttnMaps maps;
   const int64_t rows = static_cast<int64_t>(B) * TS;
@@ -1532,14 +1516,25 @@ int gather_layout(GatherArgs& g, int world, const int32_t* counts, int nmax, int
   return g.ns > 0 ? 0 : EXK_EARG;
 }
 
+// Launched as a programmatic dependent of the preceding kernel on the stream,
+// like the single-GPU merge.
 int launch_gathered(const GatherArgs& g, uint16_t* out, int device, void* stream) {
   int r = use_device(device, nullptr);
   if (r != 0) return r;
-  if (g.ns > kWideSplits)
-    merge_gathered_kernel<true><<<g.rows, wide_warps(g.ns) * 32, 0, static_cast<cudaStream_t>(stream)>>>(g, out);
-  else
-    merge_gathered_kernel<false><<<(g.rows + 3) / 4, 128, 0, static_cast<cudaStream_t>(stream)>>>(g, out);
-  return launch_status();
+  const bool wide = g.ns > kWideSplits;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(wide ? g.rows : (g.rows + 3) / 4);
+  cfg.blockDim = dim3(wide ? wide_warps(g.ns) * 32 : 128);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e =
+      cudaLaunchKernelEx(&cfg, wide ? merge_gathered_kernel<true> : merge_gathered_kernel<false>, g, out);
+  return e == cudaSuccess ? 0 : static_cast<int>(e);
 }
 
 }  // namespace

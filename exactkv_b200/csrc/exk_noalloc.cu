@@ -64,6 +64,7 @@ extern "C" int exk_attention_compressed_noalloc(const uint16_t* q, const exk_cvi
   ws.l = ws.m + rows * ns;
   ws.ns = ns;
   ws.split_len = split_len;
+  ws.heads = 0;
   if ((r = exk_attn_split_compressed(q, k, v, B, TS, Hkv, Hq, T, 0, ns, &ws, consumer_warps, qk_scale, status,
                                      device, stream)) != 0)
     return r;

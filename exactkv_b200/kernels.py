@@ -103,8 +103,9 @@ def check_status(device=None, reset=True):
 _WS = {}  # (device, stream, rows, ns) -> (o, m, l, Partials); reused by calls on the same stream
 
 
-def _workspace(device, stream, rows, ns, split_len):
-    """Split partials o [rows, ns, 128], m, l [rows, ns]."""
+def _workspace(device, stream, rows, ns, split_len, heads=0):
+    """Split partials o [rows, ns, 128], m, l [rows, ns], for a plan of ns splits
+    of split_len tokens and `heads` KV heads per work item (0: the default)."""
     key = (device.index, stream, rows, ns)
     ws = _WS.get(key)
     if ws is None:
@@ -112,6 +113,7 @@ def _workspace(device, stream, rows, ns, split_len):
         o, m, l = torch.empty(rows, ns, D, **f32), torch.empty(rows, ns, **f32), torch.empty(rows, ns, **f32)
         ws = _WS[key] = (o, m, l, Partials(o.data_ptr(), m.data_ptr(), l.data_ptr(), ns, split_len))
     ws[3].split_len = split_len
+    ws[3].heads = heads
     return ws
 
 
@@ -153,6 +155,22 @@ def attention_split(q, kc, vc, T, ws, s0, s1, num_warps=None):
                                        ctypes.byref(ws[3]), _consumer_warps(num_warps), D ** -0.5 * LOG2E,
                                        status_tensor(dev).data_ptr(), dev, stream)
     check(rc, "exk_attn_split_compressed")
+
+
+def attention_split_bf16(q, k, v, T, ws, s0, s1, num_warps=None):
+    """attention_split on uncompressed bf16 K, V [B, TS, Hkv, 128] (contiguous):
+    the same partials as the compressed kernel for the same values and plan."""
+    if k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16 or not (k.is_contiguous() and v.is_contiguous()):
+        raise ValueError("k and v must be contiguous bf16 [B, TS, Hkv, 128]")
+    TS, Hkv = k.shape[1], k.shape[2]
+    _check_q(q, T, TS)
+    B, Hq, _ = q.shape
+    dev = q.device.index
+    stream = torch.cuda.current_stream(q.device).cuda_stream
+    rc = lib.exk_attn_split_bf16(q.data_ptr(), k.data_ptr(), v.data_ptr(), B, TS, Hkv, Hq, T, s0, s1,
+                                 ctypes.byref(ws[3]), _consumer_warps(num_warps), D ** -0.5 * LOG2E,
+                                 status_tensor(dev).data_ptr(), dev, stream)
+    check(rc, "exk_attn_split_bf16")
 
 
 def merge_partials(ws, rows, out):

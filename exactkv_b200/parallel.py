@@ -55,18 +55,26 @@ class KVSplitPlan:
     bounds[r] .. bounds[r+1] are rank r's splits; token range of rank r:
     [bounds[r] * split_len, min(bounds[r+1] * split_len, T))."""
 
-    def __init__(self, B, Hkv, T, world, ns, split_len):
+    def __init__(self, B, Hkv, T, world, ns, split_len, heads=0):
         if world < 1 or ns < 1 or split_len % P != 0 or ns * split_len < T:
             raise ValueError("invalid KV-split plan")
+        if heads not in (0, 1, 2, 4, 8) or (heads and Hkv % heads):
+            raise ValueError("heads per work item must be 0 (default) or 1, 2, 4, 8 dividing Hkv")
         self.B, self.Hkv, self.T, self.world = B, Hkv, T, world
-        self.ns, self.split_len = ns, split_len
+        self.ns, self.split_len, self.heads = ns, split_len, heads
         self.bounds = [(r * ns) // world for r in range(world + 1)]
 
     @classmethod
     def make(cls, B, Hkv, T, world, device=None):
-        """The split kernel's own planner, sized for world x (SMs of one GPU) CTAs."""
+        """The split kernel's own planner, sized for world x (SMs of one GPU) CTAs,
+        with the default KV heads per work item (fewer heads per item need fewer
+        splits, but measured slower at 1 x 131072 on one and on two GPUs)."""
         ns, sl = kernels.plan_splits(B, Hkv, T, device, num_ctas=world * kernels.num_sms(device))
         return cls(B, Hkv, T, world, ns, sl)
+
+    def partials(self, o, m, l, ns):
+        """exk_partials over o, m, l with ns columns and this plan's split length and heads."""
+        return Partials(o.data_ptr(), m.data_ptr(), l.data_ptr(), ns, self.split_len, self.heads)
 
     def splits(self, rank):
         return self.bounds[rank], self.bounds[rank + 1]
@@ -101,8 +109,9 @@ def _buffers(device, stream, rows, plan):
         gathered = torch.empty(plan.world, n, dtype=torch.float32, device=device)
         local = torch.empty(n, dtype=torch.float32, device=device)
         o, m, l = block_views(local, rows, nmax)
-        bufs = _BUF[key] = (local, gathered, Partials(o.data_ptr(), m.data_ptr(), l.data_ptr(), nmax, 0))
+        bufs = _BUF[key] = (local, gathered, Partials(o.data_ptr(), m.data_ptr(), l.data_ptr(), nmax, 0, 0))
     bufs[2].split_len = plan.split_len
+    bufs[2].heads = plan.heads
     return bufs
 
 
@@ -240,8 +249,7 @@ class PeerExchange:
             off = FLAG_BYTES + par * nb * 4
             self._blocks.append((ctypes.c_void_p * self.world)(*[ptrs[p] + off for p in range(self.world)]))
             o, m, l = block_views(self.buf[head + par * nb: head + (par + 1) * nb], rows, plan.max_local)
-            self._ws.append((o, m, l, Partials(o.data_ptr(), m.data_ptr(), l.data_ptr(), plan.max_local,
-                                               plan.split_len)))
+            self._ws.append((o, m, l, plan.partials(o, m, l, plan.max_local)))
         self._counts = (ctypes.c_int32 * self.world)(*plan.counts)
         self.epoch = 0
 

@@ -70,13 +70,17 @@ typedef struct exk_cview {
 /* Split-K partials, laid out as the reference's workspace
  * (exactkv/kernels.py:290): o fp32 [rows, ns, 128] (unnormalised),
  * m fp32 [rows, ns] (running max of base-2 scores), l fp32 [rows, ns]
- * (sum of exp2(s - m)); rows = B * Hq. */
+ * (sum of exp2(s - m)); rows = B * Hq. With the plan: ns splits of split_len
+ * tokens, and `heads`, the KV heads one work item (one CTA at a time) covers:
+ * 1, 2, 4 or 8 dividing Hkv, or 0 for the default (up to 8). The partials of
+ * a split depend on `heads`, so calls that must agree bit for bit share it. */
 typedef struct exk_partials {
   float *o;
   float *m;
   float *l;
   int32_t ns;
   int32_t split_len;
+  int32_t heads;
 } exk_partials;
 
 /* Split plan: number of token splits per (sequence, KV head) and their length

@@ -166,6 +166,30 @@ def test_attention_split_subsets_match_full_run():
     kernels.check_status()
 
 
+@pytest.mark.parametrize("heads", [1, 2, 4, 8])
+def test_attention_heads_per_item(heads):
+    """A plan may set the KV heads per work item (exk_partials.heads): 1, 2 and 4
+    heads split each item's pages over the consumer warps and merge them inside
+    the CTA. Compressed == bf16 partials bit for bit, the output within
+    tolerance; T ends inside a page and the cache has forced raw rows."""
+    B, T, Hq, Hkv = 1, 20000, 32, 8
+    TS = -(-T // 16) * 16
+    k = synthetic.make_kv(B, TS, Hkv, seed=61, key=True, raw_frac=0.02)
+    v = synthetic.make_kv(B, TS, Hkv, seed=62, key=False, raw_frac=0.02)
+    q = synthetic.make_q(B, Hq, seed=63)
+    kc, vc = _compress(k), _compress(v)
+    ns, sl = 37, 544
+    ws_c = kernels._workspace(q.device, 11, B * Hq, ns, sl, heads)     # private keys
+    ws_r = kernels._workspace(q.device, 12, B * Hq, ns, sl, heads)
+    kernels.attention_split(q, kc, vc, T, ws_c, 0, ns)
+    kernels.attention_split_bf16(q, k, v, T, ws_r, 0, ns)
+    for x, y in zip(ws_c[:3], ws_r[:3]):
+        assert torch.equal(x, y)
+    out = kernels.merge_partials(ws_c, B * Hq, torch.empty_like(q))
+    _check_close(out, q, k, v, T)
+    kernels.check_status()
+
+
 def test_attention_qwen_1x32k():
     """Qwen2.5-7B shape (28 q / 4 kv), one sequence of 32,768 tokens,
     RoPE theta 1e6: compressed == bf16 bit for bit, within tolerance of float64."""

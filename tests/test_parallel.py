@@ -114,7 +114,7 @@ def _rank_caches(k, v, plan, rank):
     return caches
 
 
-def _full_run(q, k, v, T, ns, sl):
+def _full_run(q, k, v, T, ns, sl, heads=0):
     import exactkv_b200 as ekv
     from exactkv_b200 import kernels
     B, _, H, _ = k.shape
@@ -127,7 +127,7 @@ def _full_run(q, k, v, T, ns, sl):
     o = torch.empty(B * Hq, ns, D, device="cuda")
     m = torch.empty(B * Hq, ns, device="cuda")
     l = torch.empty(B * Hq, ns, device="cuda")
-    ws = (o, m, l, kernels.Partials(o.data_ptr(), m.data_ptr(), l.data_ptr(), ns, sl))
+    ws = (o, m, l, kernels.Partials(o.data_ptr(), m.data_ptr(), l.data_ptr(), ns, sl, heads))
     kernels.attention_split(q, kc, vc, T, ws, 0, ns)
     return parallel.merge(o, m, l, torch.empty_like(q))
 
@@ -148,7 +148,7 @@ def test_kv_split_emulated_ranks_bit_identical(world, B, T, Hq, Hkv):
     out = parallel.merge_gathered(gathered, plan, torch.empty_like(q))
     o, m, l = parallel.assemble(gathered, plan, rows)
     out2 = parallel.merge(o, m, l, torch.empty_like(q))
-    ref = _full_run(q, k, v, T, plan.ns, plan.split_len)
+    ref = _full_run(q, k, v, T, plan.ns, plan.split_len, plan.heads)
     kernels.check_status()
     assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
     assert torch.equal(out2.view(torch.int16), ref.view(torch.int16))
@@ -166,7 +166,7 @@ def test_peer_merge_emulated_ranks_bit_identical(world, B, T, Hq, Hkv):
     for r in range(world):
         kc, vc = _rank_caches(k, v, plan, r)
         blocks.append(parallel.local_partials(q, kc, vc, plan, r).clone())
-    ref = _full_run(q, k, v, T, plan.ns, plan.split_len)
+    ref = _full_run(q, k, v, T, plan.ns, plan.split_len, plan.heads)
     epoch = 5
     for rank in range(world):                       # every rank's view: all peers already signalled
         flags = torch.full((world,), epoch, dtype=torch.int32, device="cuda")
@@ -224,7 +224,7 @@ def _nccl_rank(rank, world, port, outdir):
         plan = KVSplitPlan.make(B, Hkv, T, world)
         kc, vc = _rank_caches(k, v, plan, rank)
         out = parallel.attention_kv_split(q, kc, vc, plan, rank)
-        ref = _full_run(q, k, v, T, plan.ns, plan.split_len)
+        ref = _full_run(q, k, v, T, plan.ns, plan.split_len, plan.heads)
         kernels.check_status()
         ok = torch.equal(out.view(torch.int16), ref.view(torch.int16))
         # the peer merge over symmetric memory: several calls (both blocks of
@@ -233,7 +233,7 @@ def _nccl_rank(rank, world, port, outdir):
         for i in range(5):
             qi = synthetic.make_q(B, Hq, seed=300 + i, device="cuda")
             got = ex.attention(qi, kc, vc)
-            want = _full_run(qi, k, v, T, plan.ns, plan.split_len)
+            want = _full_run(qi, k, v, T, plan.ns, plan.split_len, plan.heads)
             kernels.check_status()
             ok = ok and torch.equal(got.view(torch.int16), want.view(torch.int16))
         ex.close()
