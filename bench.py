@@ -33,6 +33,11 @@ ahead with one host sync per 8 pages instead of a sync per page) and copies
 the output back to pinned host memory; the context grows by one token per
 step.
 
+other_configs: BASELINE configs[1] (Qwen 1 x 32768) and Llama 8 x 8192 (the second
+shape of configs[2]): per-call µs, compressed TB/s and the bf16 sibling's µs,
+with an L2 flush before each call. kv_split: configs[3] (1 x 131072 split by KV
+sequence over the ranks).
+
 engine: BASELINE configs[4] decode throughput through exactkv_b200.Engine on a
 random-init Llama-3.1-8B (32 layers, hidden 4096, 32 q / 8 kv heads, FFN 14336,
 vocab 128256, bf16 weights ~ N(0, 0.02)), batch sized to the free HBM minus
@@ -77,6 +82,7 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-engine", action="store_true")
     ap.add_argument("--no-kv-split", action="store_true")
+    ap.add_argument("--no-configs", action="store_true")
     ap.add_argument("--engine-steps", type=int, default=24)
     ap.add_argument("--num-warps", type=int, default=8)
     ap.add_argument("--quick", action="store_true",
@@ -307,6 +313,10 @@ def run_ours(a, rank, world, local):
 
     encoder = None if a.quick else time_encoder(kbf, B, T, Hkv, dev)
 
+    configs = None
+    if not (a.no_configs or a.quick):
+        configs = run_configs(a, dev, world)
+
     kv_split = None
     if not (a.no_kv_split or a.quick):
         kv_split = run_kv_split(a, dev, rank, world)
@@ -350,6 +360,7 @@ def run_ours(a, rank, world, local):
         "clocks": clocks.summary(),
         "e2e": e2e,
         "engine": engine,
+        "other_configs": configs,
         "kv_split": kv_split,
         "cpu_baseline": cpu,
     }
@@ -470,6 +481,65 @@ def run_e2e(a, kc, vc, B, Hq, Hkv, T0, dev, world, raw_rows0, ns0):
                     "device-length step (append + page encode at boundaries, decode attention, length advance; "
                     "pools kept ahead with one sync per 8 pages), D2H output into pinned memory; "
                     "context grows from 4096"}
+
+
+def run_configs(a, dev, world, reps=30):
+    """BASELINE configs[1] (Qwen2.5-7B 1 x 32768, 28 q / 4 kv, RoPE theta 1e6) and
+    the second shape of configs[2] (Llama 8 x 8192, 32 q / 8 kv): one
+    decode-attention call through the public API, compressed and on the bf16
+    sibling, each call's device time with a 256 MB L2 flush before it (the Qwen
+    cache fits in L2); median over reps, this rank's replica."""
+    import torch
+    import torch.distributed as dist
+
+    import exactkv_b200 as ekv
+    from exactkv_b200 import kernels, synthetic
+
+    peak, _ = load_peak()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    out = {}
+    for name, (B, T, Hq, Hkv, theta) in {"qwen2.5-7b_1x32768": (1, 32768, 28, 4, 1e6),
+                                         "llama3.1-8b_8x8192": (8, 8192, 32, 8, 5e5)}.items():
+        k = synthetic.make_kv(B, T, Hkv, seed=700, theta=theta, key=True, device=dev)
+        v = synthetic.make_kv(B, T, Hkv, seed=701, theta=theta, key=False, device=dev)
+        q = synthetic.make_q(B, Hq, seed=702, device=dev)
+        kc, vc = ekv.CompressedKV(B, T, Hkv, 128, device=dev), ekv.CompressedKV(B, T, Hkv, 128, device=dev)
+        for b in range(B):
+            kc.prefill_slot(b, k[b:b + 1])
+            vc.prefill_slot(b, v[b:b + 1])
+        ns, _ = kernels.plan_splits(B, Hkv, T, dev)
+        nbytes, raw_rows = algorithmic_bytes(kc, vc, B, Hkv, Hq, T, ns)
+
+        def per_call(fn):
+            for _ in range(3):
+                fn()
+            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize(dev)
+            for e0, e1 in ev:
+                flush.zero_()
+                e0.record(stream)
+                fn()
+                e1.record(stream)
+            torch.cuda.synchronize(dev)
+            return statistics.median(e0.elapsed_time(e1) for e0, e1 in ev) * 1e3
+
+        us_c = per_call(lambda: ekv.decode_attention(q, kc, vc, num_warps=a.num_warps))
+        us_r = per_call(lambda: kernels.attention_reference(q, k, v, T, num_warps=a.num_warps))
+        kernels.check_status(dev)
+        tbs = nbytes / (us_c * 1e-6) / 1e12
+        out[name] = {"batch": B, "context": T, "q_heads": Hq, "kv_heads": Hkv, "splits": ns,
+                     "us_per_call": round(us_c, 2), "compressed_tbs": round(tbs, 3),
+                     "frac_of_measured_peak": round(tbs * 1e3 / peak, 4),
+                     "bf16_equiv_tbs": round(2 * B * T * Hkv * 256 / (us_c * 1e-6) / 1e12, 3),
+                     "bf16_sibling_us_per_call": round(us_r, 2), "speedup_vs_bf16_sibling": round(us_r / us_c, 3),
+                     "raw_row_fraction": round(raw_rows / (2 * B * T * Hkv), 5)}
+        del k, v, q, kc, vc
+        torch.cuda.empty_cache()
+    out["timing"] = "CUDA events around each call (split + merge), 256 MB L2 flush before each, median"
+    return out
 
 
 def run_kv_split(a, dev, rank, world, T=131072, Hq=32, Hkv=8, reps=20):
