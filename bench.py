@@ -544,10 +544,11 @@ def run_configs(a, dev, world, reps=30):
 
 def run_kv_split(a, dev, rank, world, T=131072, Hq=32, Hkv=8, reps=20):
     """one sequence of 131072 tokens (2% forced raw rows) split
-    over the ranks by KV sequence; per call: the split kernel writing the rank's
-    partial block into symmetric memory, then the peer merge reading every
-    rank's block over NVLink (exactkv_b200.parallel.PeerExchange); the NCCL
-    all-gather variant is timed beside it."""
+    over the ranks by KV sequence; per call: the split kernel, the rank's group
+    partial (one per row) written into symmetric memory, then the peer merge
+    reading every rank's group partial over NVLink
+    (exactkv_b200.parallel.PeerExchange); the NCCL all-gather variant is timed
+    beside it."""
     import torch
     import torch.distributed as dist
 
@@ -632,9 +633,10 @@ def run_kv_split(a, dev, rank, world, T=131072, Hq=32, Hkv=8, reps=20):
             "phases_us_rank0": phases, "context": T, "ranks": world, "splits": plan.ns,
             "split_len": plan.split_len, "tokens_per_rank": n, "compressed_mb_per_rank": round(nbytes / 1e6, 1),
             "what": "1 x 131072 decode attention (32 q / 8 kv, 2% raw rows) split by KV sequence over the ranks: "
-                    "split kernel into the rank's symmetric-memory block, then the peer merge reading every rank's "
-                    "block over NVLink in split order (max over ranks); nccl_all_gather_us_per_call: the same with "
-                    "NCCL all_gather_into_tensor and the gathered merge"}
+                    "split kernel, the rank's splits merged to one group partial per row in its symmetric-memory "
+                    "block, then the peer merge reading every rank's group partial over NVLink in rank order (max "
+                    "over ranks); nccl_all_gather_us_per_call: the same with NCCL all_gather_into_tensor of the "
+                    "group partials and the gathered merge"}
 
 
 def run_engine(a, dev, world, context=4096, warm=4):

@@ -542,14 +542,43 @@ __device__ __forceinline__ void load_q(const AttnArgs& a, int b, int hk, int g, 
 // ------------------------------------------------------------------ split merge
 
 // Partials of one workspace: o [rows, ns, 128], m, l [rows, ns].
+// Partials of one workspace: o [rows, ns, 128], m, l [rows, ns]; split s of
+// the locator is column s0 + s.
 struct WsSplits {
   const float* o_;
   const float* m_;
   const float* l_;
-  int64_t row, ns;
-  __device__ const float* m(int s) const { return m_ + row * ns + s; }
-  __device__ const float* l(int s) const { return l_ + row * ns + s; }
-  __device__ const float4* o(int s) const { return reinterpret_cast<const float4*>(o_ + (row * ns + s) * kD); }
+  int64_t row, ns, s0;
+  __device__ const float* m(int s) const { return m_ + row * ns + s0 + s; }
+  __device__ const float* l(int s) const { return l_ + row * ns + s0 + s; }
+  __device__ const float4* o(int s) const { return reinterpret_cast<const float4*>(o_ + (row * ns + s0 + s) * kD); }
+};
+
+// Where a merged row goes. Bf16Out: the attention output, acc / den in bf16.
+// PartialOut: the partial of the union of the merged splits, in the layout of
+// one split's partial (o = acc unnormalised, m = the splits' maximum M, l =
+// den), which a later merge combines with others like any split.
+struct Bf16Out {
+  uint16_t* row;
+  __device__ void put(int lane, float4 acc, float den, float) const {
+    uint2 r;
+    r.x = pack_bf16x2(acc.x / den, acc.y / den);
+    r.y = pack_bf16x2(acc.z / den, acc.w / den);
+    reinterpret_cast<uint2*>(row)[lane] = r;
+  }
+};
+
+struct PartialOut {
+  float* o;
+  float* m;
+  float* l;
+  __device__ void put(int lane, float4 acc, float den, float M) const {
+    reinterpret_cast<float4*>(o)[lane] = acc;
+    if (lane == 0) {
+      *m = M;
+      *l = den;
+    }
+  }
 };
 
 constexpr int kMaxRanks = 16;
@@ -652,8 +681,8 @@ __device__ __forceinline__ bool peers_ready(const GatherArgs& g) {
 // of split s of the row (m, l and the lane's float4 of o), so partials laid out
 // by one workspace or gathered from several GPUs merge with the same
 // arithmetic, bit for bit.
-template <class Loc>
-__device__ __forceinline__ void merge_row(const Loc& loc, int ns, int lane, uint16_t* __restrict__ out_row) {
+template <class Loc, class Out>
+__device__ __forceinline__ void merge_row(const Loc& loc, int ns, int lane, const Out& out) {
   const float mv = lane < ns ? __ldcg(loc.m(lane)) : -INFINITY;
   const float lv = lane < ns ? __ldcg(loc.l(lane)) : 0.f;
   float4 v[16];
@@ -662,7 +691,8 @@ __device__ __forceinline__ void merge_row(const Loc& loc, int ns, int lane, uint
   float M = mv;
 #pragma unroll
   for (int d = 16; d > 0; d >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, d));
-  const float w = lane < ns ? ex2(mv - M) : 0.f;
+  // an empty split (m = -inf) weighs 0, also when every split is empty
+  const float w = lane < ns && mv != -INFINITY ? ex2(mv - M) : 0.f;
   float den = lane < ns ? w * lv : 0.f;
 #pragma unroll
   for (int d = 16; d > 0; d >>= 1) den += __shfl_xor_sync(0xFFFFFFFFu, den, d);
@@ -677,10 +707,7 @@ __device__ __forceinline__ void merge_row(const Loc& loc, int ns, int lane, uint
       acc.w += wu * v[u].w;
     }
   }
-  uint2 r;
-  r.x = pack_bf16x2(acc.x / den, acc.y / den);
-  r.y = pack_bf16x2(acc.z / den, acc.w / den);
-  reinterpret_cast<uint2*>(out_row)[lane] = r;
+  out.put(lane, acc, den, M);
 }
 
 // Splits above which a row is merged by a whole CTA instead of one warp.
@@ -703,8 +730,8 @@ __host__ __device__ constexpr int wide_warps(int ns) {
 // combines the warps in warp order, each scaled by 2^(its max - the row's).
 // Splits with m = -inf (past a sequence's length) weigh 0. The order depends
 // only on ns, so every caller with the same splits gets the same bits.
-template <class Loc>
-__device__ __forceinline__ void merge_row_wide(const Loc& loc, int ns, uint16_t* __restrict__ out_row) {
+template <class Loc, class Out>
+__device__ __forceinline__ void merge_row_wide(const Loc& loc, int ns, const Out& out) {
   __shared__ float s_max[kWideMaxWarps], s_den[kWideMaxWarps];
   __shared__ float4 s_acc[kWideMaxWarps][32];
   const int nw = wide_warps(ns);
@@ -763,10 +790,7 @@ __device__ __forceinline__ void merge_row_wide(const Loc& loc, int ns, uint16_t*
     acc.w += f * t.w;
     den += f * s_den[i];
   }
-  uint2 r;
-  r.x = pack_bf16x2(acc.x / den, acc.y / den);
-  r.y = pack_bf16x2(acc.z / den, acc.w / den);
-  reinterpret_cast<uint2*>(out_row)[lane] = r;
+  out.put(lane, acc, den, M);
 }
 
 // ------------------------------------------------------------------ kernel
@@ -1138,11 +1162,11 @@ __global__ void __launch_bounds__(WIDE ? kWideMaxWarps * 32 : 128)
   if (advance != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *advance += n_adv;
   if constexpr (WIDE) {
     const int row = blockIdx.x;
-    merge_row_wide(WsSplits{o, m, l, row, ns}, ns, out + static_cast<int64_t>(row) * kD);
+    merge_row_wide(WsSplits{o, m, l, row, ns, 0}, ns, Bf16Out{out + static_cast<int64_t>(row) * kD});
   } else {
     const int row = blockIdx.x * 4 + (threadIdx.x >> 5);
     if (row >= rows) return;
-    merge_row(WsSplits{o, m, l, row, ns}, ns, threadIdx.x & 31, out + static_cast<int64_t>(row) * kD);
+    merge_row(WsSplits{o, m, l, row, ns, 0}, ns, threadIdx.x & 31, Bf16Out{out + static_cast<int64_t>(row) * kD});
   }
 }
 
@@ -1158,11 +1182,30 @@ __global__ void __launch_bounds__(WIDE ? kWideMaxWarps * 32 : 128)
   if (g.flags != nullptr && !peers_ready(g)) return;
   if constexpr (WIDE) {
     const int row = blockIdx.x;
-    merge_row_wide(GatheredSplits{&g, row}, g.ns, out + static_cast<int64_t>(row) * kD);
+    merge_row_wide(GatheredSplits{&g, row}, g.ns, Bf16Out{out + static_cast<int64_t>(row) * kD});
   } else {
     const int row = blockIdx.x * 4 + (threadIdx.x >> 5);
     if (row >= g.rows) return;
-    merge_row(GatheredSplits{&g, row}, g.ns, threadIdx.x & 31, out + static_cast<int64_t>(row) * kD);
+    merge_row(GatheredSplits{&g, row}, g.ns, threadIdx.x & 31, Bf16Out{out + static_cast<int64_t>(row) * kD});
+  }
+}
+
+// Splits [s0, s0 + n) of a workspace merged into one partial per row
+// (PartialOut): po [rows, 128], pm, pl [rows].
+template <bool WIDE>
+__global__ void __launch_bounds__(WIDE ? kWideMaxWarps * 32 : 128)
+    merge_partial_kernel(const float* __restrict__ o, const float* __restrict__ m, const float* __restrict__ l,
+                         int ns, int s0, int n, int rows, float* __restrict__ po, float* __restrict__ pm,
+                         float* __restrict__ pl) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if constexpr (WIDE) {
+    const int row = blockIdx.x;
+    merge_row_wide(WsSplits{o, m, l, row, ns, s0}, n, PartialOut{po + static_cast<int64_t>(row) * kD, pm + row, pl + row});
+  } else {
+    const int row = blockIdx.x * 4 + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    merge_row(WsSplits{o, m, l, row, ns, s0}, n, threadIdx.x & 31,
+              PartialOut{po + static_cast<int64_t>(row) * kD, pm + row, pl + row});
   }
 }
 
@@ -1538,6 +1581,32 @@ int launch_gathered(const GatherArgs& g, uint16_t* out, int device, void* stream
 }
 
 }  // namespace
+
+extern "C" int exk_attn_merge_partial(const exk_partials* ws, int rows, int s0, int s1, float* o, float* m, float* l,
+                                      int device, void* stream) {
+  if (ws == nullptr || o == nullptr || m == nullptr || l == nullptr || rows <= 0) return EXK_EARG;
+  if (s0 < 0 || s1 > ws->ns || s0 >= s1) return EXK_EARG;
+  if (!aligned16(ws->o) || !aligned16(o)) return EXK_EALIGN;
+  int r = use_device(device, nullptr);
+  if (r != 0) return r;
+  const int n = s1 - s0;
+  const bool wide = n > kWideSplits;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(wide ? rows : (rows + 3) / 4);
+  cfg.blockDim = dim3(wide ? wide_warps(n) * 32 : 128);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, wide ? merge_partial_kernel<true> : merge_partial_kernel<false>,
+                                           static_cast<const float*>(ws->o), static_cast<const float*>(ws->m),
+                                           static_cast<const float*>(ws->l), static_cast<int>(ws->ns), s0, n, rows, o,
+                                           m, l);
+  return e == cudaSuccess ? 0 : static_cast<int>(e);
+}
 
 extern "C" int exk_attn_merge_gathered(const float* buf, int world, const int32_t* counts, int nmax, int rows,
                                        uint16_t* out, int device, void* stream) {

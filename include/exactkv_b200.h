@@ -114,6 +114,15 @@ int exk_attn_split_bf16(const uint16_t *q, const uint16_t *k, const uint16_t *v,
  * Replaces _reduce_kernel (exactkv/kernels.py:33-43). */
 int exk_attn_merge(const exk_partials *ws, int rows, uint16_t *out, int device, void *stream);
 
+/* Splits [s0, s1) of `ws` merged into one partial per row, the partial of the
+ * union of those splits in the layout of a single split's: o [rows, 128]
+ * (unnormalised), m [rows] (their maximum), l [rows]. A later merge combines
+ * such partials like splits. The KV-sequence split reduces each GPU's run of
+ * splits this way, so the GPUs exchange one partial per row each. No
+ * counterpart in the reference. */
+int exk_attn_merge_partial(const exk_partials *ws, int rows, int s0, int s1, float *o, float *m, float *l,
+                           int device, void *stream);
+
 /* Merge of split partials all-gathered from the `world` GPUs of a KV-sequence
  * split (world <= 16), straight from the gathered buffer: rank r's block (rows
  * * nmax * 130 floats rounded up to a multiple of 4, so each block starts

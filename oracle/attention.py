@@ -72,6 +72,17 @@ def merge(o, m, l):
     return (o * w[..., None]).sum(-2) / (l * w).sum(-1)[..., None]
 
 
+def merge_group(o, m, l):
+    """The partial of a run of splits (the last axis of m, l; o [..., n, D]):
+    M = max_s m_s, o_g = sum_s o_s 2^(m_s - M), l_g = sum_s l_s 2^(m_s - M), in
+    the layout of one split's partial, so merge() combines groups like splits
+    (the two-level merge of a KV-sequence split; no counterpart in the
+    reference, whose merge is _reduce_kernel, exactkv/kernels.py:33-43)."""
+    M = m.max(-1)
+    w = np.where(np.isneginf(m), np.float32(0), np.exp2(m - M[..., None]))
+    return (o * w[..., None]).sum(-2).astype(np.float32), M.astype(np.float32), (l * w).sum(-1).astype(np.float32)
+
+
 def attention(q_bits, k_bits, v_bits, T, block_n=64):
     """Reference split-K decode attention; returns bf16 bit patterns [B, Hq, D]."""
     o, m, l = split_partials(q_bits, k_bits, v_bits, T, block_n)

@@ -1,15 +1,17 @@
-"""KV-sequence split over ranks (exactkv_b200.parallel).
+"""KV-sequence split over ranks (exactkv_b200.parallel): two-level merge.
 
-CPU (gloo, world size 2 and 3): each rank computes its splits' partials with the
-oracle, the flat partial blocks go through the real all-gather and assemble code,
-and the merge of the gathered partials must equal the single-process oracle
-bit for bit (partials depend only on their split's tokens).
+CPU (gloo, world size 2 and 3): each rank computes its splits' partials and
+their group partial with the oracle, the blocks go through the real all-gather
+and assemble code, and the merge of the gathered group partials must equal the
+single-process oracle running the same two levels bit for bit (partials depend
+only on their split's tokens).
 GPU: ranks emulated one after another on one GPU (every rank's cache holds only
 its own pages) must be bit-identical to one kernel run over the whole cache
-with the same plan, through the gathered merge and through the peer merge
-(flags already set, so nothing waits); the peer merge's wait on a flag that
-nothing sets gives up with its status code; with two or more GPUs, the same
-through NCCL and through symmetric-memory peer reads.
+with the same plan and the same two levels, through the gathered merge and
+through the peer merge (flags already set, so nothing waits), and within
+tolerance of float64 attention; the peer merge's wait on a flag that nothing
+sets gives up with its status code; with two or more GPUs, the same through
+NCCL and through symmetric-memory peer reads.
 """
 import os
 import socket
@@ -23,7 +25,7 @@ import torch.multiprocessing as mp
 from exactkv_b200 import parallel
 from exactkv_b200.parallel import KVSplitPlan, block_floats, block_views
 from oracle import attention as oatt
-from oracle.bf16 import f32_to_bits
+from oracle.bf16 import bits_to_f32, f32_to_bits
 from oracle.synth import synth_kv, synth_q
 
 D = 128
@@ -50,19 +52,36 @@ def test_plan_partition_covers_every_split_once():
 
 
 def _oracle_block(qb, kb, vb, plan, rank):
-    """One rank's flat block of partials, computed by the oracle over the rank's tokens only."""
+    """One rank's flat block: the group partial of its splits, by the oracle over
+    the rank's tokens only."""
     t0, t1 = plan.tokens(rank)
     B, Hq, _ = qb.shape
     rows = B * Hq
-    flat = torch.zeros(block_floats(rows, plan.max_local), dtype=torch.float32)
+    flat = torch.zeros(block_floats(rows), dtype=torch.float32)
     n = plan.count(rank)
     if n:
         o, m, l = oatt.split_partials(qb, kb[:, t0:t1], vb[:, t0:t1], t1 - t0, splits=(n, plan.split_len))
-        bo, bm, bl = block_views(flat, rows, plan.max_local)
-        bo[:, :n] = torch.from_numpy(o.reshape(rows, n, D))
-        bm[:, :n] = torch.from_numpy(m.reshape(rows, n))
-        bl[:, :n] = torch.from_numpy(l.reshape(rows, n))
+        go, gm, gl = oatt.merge_group(o.reshape(rows, n, D), m.reshape(rows, n), l.reshape(rows, n))
+        bo, bm, bl = block_views(flat, rows)
+        bo[:, 0] = torch.from_numpy(go)
+        bm[:, 0] = torch.from_numpy(gm)
+        bl[:, 0] = torch.from_numpy(gl)
     return flat
+
+
+def _oracle_two_level(qb, kb, vb, T, plan):
+    """The single-process oracle: all splits, each rank's run merged to its group
+    partial, the groups merged in rank order."""
+    B, Hq, _ = qb.shape
+    rows = B * Hq
+    o, m, l = oatt.split_partials(qb, kb, vb, T, splits=(plan.ns, plan.split_len))
+    o, m, l = o.reshape(rows, plan.ns, D), m.reshape(rows, plan.ns), l.reshape(rows, plan.ns)
+    groups = [oatt.merge_group(o[:, a:a + n], m[:, a:a + n], l[:, a:a + n])
+              for a, n in zip(plan.bounds, plan.counts) if n]
+    go = np.stack([g[0] for g in groups], 1)
+    gm = np.stack([g[1] for g in groups], 1)
+    gl = np.stack([g[2] for g in groups], 1)
+    return f32_to_bits(oatt.merge(go, gm, gl)).reshape(B, Hq, D)
 
 
 def _gloo_rank(rank, world, port, args, outdir):
@@ -90,11 +109,14 @@ def test_kv_split_gloo_bit_identical(world, B, T, Hq, Hkv, ns, sl):
                            start_method="spawn")
         outs = [np.load(os.path.join(d, f"out{r}.npy")) for r in range(world)]
     qb, kb, vb = synth_q(11, B, Hq), synth_kv(12, B, T, Hkv), synth_kv(13, B, T, Hkv, key=False)
-    o, m, l = oatt.split_partials(qb, kb, vb, T, splits=(ns, sl))
-    ref = f32_to_bits(oatt.merge(o.reshape(B * Hq, ns, D), m.reshape(B * Hq, ns),
-                                 l.reshape(B * Hq, ns))).reshape(B, Hq, D)
+    plan = KVSplitPlan(B, Hkv, T, world, ns, sl)
+    ref = _oracle_two_level(qb, kb, vb, T, plan)
     for out in outs:
         assert np.array_equal(out, ref)
+    # and the two-level result is the attention: within tolerance of float64
+    f64 = oatt.attention_f64(qb, kb, vb, T)
+    got = bits_to_f32(ref).astype(np.float64)
+    assert (np.abs(got - f64) / oatt.tolerance(qb, kb, vb, T, f64)).max() <= 1.0
 
 
 # ------------------------------------------------------------------ GPU
@@ -114,7 +136,8 @@ def _rank_caches(k, v, plan, rank):
     return caches
 
 
-def _full_run(q, k, v, T, ns, sl, heads=0):
+def _full_run(q, k, v, T, plan):
+    """One GPU, the whole cache: every split of the plan, then its two levels."""
     import exactkv_b200 as ekv
     from exactkv_b200 import kernels
     B, _, H, _ = k.shape
@@ -124,12 +147,21 @@ def _full_run(q, k, v, T, ns, sl, heads=0):
         kc.prefill_slot(b, k[b:b + 1, :T].contiguous())
         vc.prefill_slot(b, v[b:b + 1, :T].contiguous())
     Hq = q.shape[1]
+    ns = plan.ns
     o = torch.empty(B * Hq, ns, D, device="cuda")
     m = torch.empty(B * Hq, ns, device="cuda")
     l = torch.empty(B * Hq, ns, device="cuda")
-    ws = (o, m, l, kernels.Partials(o.data_ptr(), m.data_ptr(), l.data_ptr(), ns, sl, heads))
+    ws = (o, m, l, plan.partials(o, m, l, ns))
     kernels.attention_split(q, kc, vc, T, ws, 0, ns)
-    return parallel.merge(o, m, l, torch.empty_like(q))
+    return parallel.merge_two_level(ws, plan, B * Hq, torch.empty_like(q))
+
+
+def _check_f64(out, q, k, v, T):
+    from gpu_util import to_bits
+    qb, kb, vb = to_bits(q), to_bits(k[:, :T]), to_bits(v[:, :T])
+    f64 = oatt.attention_f64(qb, kb, vb, T)
+    got = bits_to_f32(to_bits(out)).astype(np.float64)
+    assert (np.abs(got - f64) / oatt.tolerance(qb, kb, vb, T, f64)).max() <= 1.0
 
 
 @pytest.mark.gpu
@@ -141,17 +173,19 @@ def test_kv_split_emulated_ranks_bit_identical(world, B, T, Hq, Hkv):
     q = synthetic.make_q(B, Hq, seed=23, device="cuda")
     plan = KVSplitPlan.make(B, Hkv, T, world)
     rows = B * Hq
-    gathered = torch.full((world, block_floats(rows, plan.max_local)), float("nan"), device="cuda")
+    gathered = torch.full((world, block_floats(rows)), float("nan"), device="cuda")
     for r in range(world):
         kc, vc = _rank_caches(k, v, plan, r)
-        gathered[r] = parallel.local_partials(q, kc, vc, plan, r)
+        parallel.local_partials(q, kc, vc, plan, r, out=gathered[r])
     out = parallel.merge_gathered(gathered, plan, torch.empty_like(q))
     o, m, l = parallel.assemble(gathered, plan, rows)
     out2 = parallel.merge(o, m, l, torch.empty_like(q))
-    ref = _full_run(q, k, v, T, plan.ns, plan.split_len, plan.heads)
+    ref = _full_run(q, k, v, T, plan)
     kernels.check_status()
     assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
     assert torch.equal(out2.view(torch.int16), ref.view(torch.int16))
+    if T <= 8192:
+        _check_f64(out, q, k, v, T)
 
 
 @pytest.mark.gpu
@@ -166,7 +200,7 @@ def test_peer_merge_emulated_ranks_bit_identical(world, B, T, Hq, Hkv):
     for r in range(world):
         kc, vc = _rank_caches(k, v, plan, r)
         blocks.append(parallel.local_partials(q, kc, vc, plan, r).clone())
-    ref = _full_run(q, k, v, T, plan.ns, plan.split_len, plan.heads)
+    ref = _full_run(q, k, v, T, plan)
     epoch = 5
     for rank in range(world):                       # every rank's view: all peers already signalled
         flags = torch.full((world,), epoch, dtype=torch.int32, device="cuda")
@@ -224,7 +258,7 @@ def _nccl_rank(rank, world, port, outdir):
         plan = KVSplitPlan.make(B, Hkv, T, world)
         kc, vc = _rank_caches(k, v, plan, rank)
         out = parallel.attention_kv_split(q, kc, vc, plan, rank)
-        ref = _full_run(q, k, v, T, plan.ns, plan.split_len, plan.heads)
+        ref = _full_run(q, k, v, T, plan)
         kernels.check_status()
         ok = torch.equal(out.view(torch.int16), ref.view(torch.int16))
         # the peer merge over symmetric memory: several calls (both blocks of
@@ -233,7 +267,7 @@ def _nccl_rank(rank, world, port, outdir):
         for i in range(5):
             qi = synthetic.make_q(B, Hq, seed=300 + i, device="cuda")
             got = ex.attention(qi, kc, vc)
-            want = _full_run(qi, k, v, T, plan.ns, plan.split_len, plan.heads)
+            want = _full_run(qi, k, v, T, plan)
             kernels.check_status()
             ok = ok and torch.equal(got.view(torch.int16), want.view(torch.int16))
         ex.close()
