@@ -20,7 +20,7 @@ bf16-equivalent bytes are 2 x B x T x Hkv x 256.
 
 Timing: W warm-up steps, then K steps between two barriers + synchronize,
 timed with CUDA events on the launching stream; the cache (~425 MB) exceeds the
-126 MB L2, and a second pass with a 256 MB L2 flush between launches is
+126 MB L2, and a second pass with the L2 evicted between launches (a 256 MB read) is
 reported as a cross-check of the per-launch kernel time. SM clocks and throttle
 reasons are sampled through NVML every 5 ms during warm-up and timing.
 
@@ -35,7 +35,10 @@ step.
 
 other_configs: BASELINE configs[1] (Qwen 1 x 32768) and Llama 8 x 8192 (the second
 shape of configs[2]): per-call µs, compressed TB/s and the bf16 sibling's µs,
-with an L2 flush before each call. kv_split: configs[3] (1 x 131072 split by KV
+with the L2 evicted before each call.
+
+FlashInfer (installed library, comparison only): its TRT-LLM-gen bf16 paged
+decode on the same bf16 K/V (16-token pages), timed like our calls. kv_split: configs[3] (1 x 131072 split by KV
 sequence over the ranks).
 
 engine: BASELINE configs[4] decode throughput through exactkv_b200.Engine on a
@@ -203,6 +206,38 @@ def algorithmic_bytes(kc, vc, B, Hkv, Hq, T, ns):
     return total, raw_rows
 
 
+def l2_flush(buf):
+    """Evicts the L2 (126 MB) by reading a 256 MB buffer: the lines it leaves are
+    clean, so no write-back lands in the next timed kernel (a write flush would)."""
+    buf.view(-1, 1 << 20).amax(dim=1)
+
+
+def flashinfer_decode(q, k, v, T):
+    """FlashInfer's TRT-LLM-gen bf16 paged decode (B200 kernels shipped prebuilt
+    with flashinfer) over the same bf16 K, V viewed as 16-token pages in NHD
+    layout; a speed comparison only, never part of the product. Returns a
+    zero-argument call, or None with the reason when FlashInfer is unavailable."""
+    import torch
+    try:
+        import flashinfer
+        B, TS, Hkv, D = k.shape
+        npg = TS // 16
+        kp, vp = k.view(B * npg, 16, Hkv, D), v.view(B * npg, 16, Hkv, D)
+        tables = torch.arange(B * npg, dtype=torch.int32, device=q.device).view(B, npg)
+        lens = torch.full((B,), T, dtype=torch.int32, device=q.device)
+        ws = torch.zeros(128 << 20, dtype=torch.uint8, device=q.device)
+
+        def call():
+            return flashinfer.decode.trtllm_batch_decode_with_kv_cache(q, (kp, vp), ws, tables, lens, T,
+                                                                       bmm1_scale=D ** -0.5, bmm2_scale=1.0,
+                                                                       kv_layout="NHD")
+        call()
+        torch.cuda.synchronize(q.device)
+        return call, None
+    except Exception as e:  # noqa: BLE001 - reported as unavailable
+        return None, f"{type(e).__name__}: {str(e)[:160]}"
+
+
 def run_ours(a, rank, world, local):
     import torch
     import torch.distributed as dist
@@ -265,7 +300,7 @@ def run_ours(a, rank, world, local):
         t0.record(stream)
         for i in range(K):
             if flush_between:
-                flush.zero_()
+                l2_flush(flush)
             if per_launch:
                 fn(*evs[i])
             else:
@@ -305,6 +340,14 @@ def run_ours(a, rank, world, local):
         sibling_step()
     sib_ms, _ = timed(sibling_step, a.steps)
     sib_us = sib_ms / a.steps * 1e3
+    fi_call, fi_why = flashinfer_decode(q, kbf, vbf, T) if not a.quick else (None, "skipped (--quick)")
+    fi_us = None
+    if fi_call is not None:
+        for _ in range(3):
+            fi_call()
+        fi_ms, _ = timed(fi_call, a.steps)
+        fi_us = round(fi_ms / a.steps * 1e3, 2)
+    fi_call = None                       # holds views of the bf16 cache, freed before the engine leg
 
     value = nbytes * a.steps * world / (total_ms * 1e-3) / 1e12
     peak, peak_src = load_peak()
@@ -352,6 +395,8 @@ def run_ours(a, rank, world, local):
         "frac_of_nominal_8tbs": round(value / world / (NOMINAL_HBM_GBS / 1e3), 4),
         "bf16_sibling_us_per_call": round(sib_us, 2),
         "speedup_vs_bf16_sibling": round(sib_us / (ms_per_step * 1e3), 3),
+        "flashinfer_trtllm_bf16_us_per_call": fi_us if fi_us is not None else fi_why,
+        "speedup_vs_flashinfer_bf16": round(fi_us / (ms_per_step * 1e3), 3) if fi_us is not None else None,
         "roofline": {"bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved_gbs / peak, 4), "peak_source": f"{peak_src} hbm_gbs (copy, read+write)",
                      "traffic": traffic, "kernel": "exk::attn_split_kernel<compressed>"},
@@ -519,7 +564,7 @@ def run_configs(a, dev, world, reps=30):
                 dist.barrier()
             torch.cuda.synchronize(dev)
             for e0, e1 in ev:
-                flush.zero_()
+                l2_flush(flush)
                 e0.record(stream)
                 fn()
                 e1.record(stream)
@@ -528,6 +573,9 @@ def run_configs(a, dev, world, reps=30):
 
         us_c = per_call(lambda: ekv.decode_attention(q, kc, vc, num_warps=a.num_warps))
         us_r = per_call(lambda: kernels.attention_reference(q, k, v, T, num_warps=a.num_warps))
+        fi_call, fi_why = flashinfer_decode(q, k, v, T)
+        us_f = per_call(fi_call) if fi_call is not None else None
+        fi_call = None
         kernels.check_status(dev)
         tbs = nbytes / (us_c * 1e-6) / 1e12
         out[name] = {"batch": B, "context": T, "q_heads": Hq, "kv_heads": Hkv, "splits": ns,
@@ -535,10 +583,13 @@ def run_configs(a, dev, world, reps=30):
                      "frac_of_measured_peak": round(tbs * 1e3 / peak, 4),
                      "bf16_equiv_tbs": round(2 * B * T * Hkv * 256 / (us_c * 1e-6) / 1e12, 3),
                      "bf16_sibling_us_per_call": round(us_r, 2), "speedup_vs_bf16_sibling": round(us_r / us_c, 3),
+                     "flashinfer_trtllm_bf16_us_per_call": round(us_f, 2) if us_f is not None else fi_why,
+                     "speedup_vs_flashinfer_bf16": round(us_f / us_c, 3) if us_f is not None else None,
                      "raw_row_fraction": round(raw_rows / (2 * B * T * Hkv), 5)}
         del k, v, q, kc, vc
         torch.cuda.empty_cache()
-    out["timing"] = "CUDA events around each call (split + merge), 256 MB L2 flush before each, median"
+    out["timing"] = ("CUDA events around each call (ours: split + merge), L2 evicted before each by reading a "
+                     "256 MB buffer, median")
     return out
 
 

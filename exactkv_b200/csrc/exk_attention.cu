@@ -541,7 +541,6 @@ __device__ __forceinline__ void load_q(const AttnArgs& a, int b, int hk, int g, 
 
 // ------------------------------------------------------------------ split merge
 
-// Partials of one workspace: o [rows, ns, 128], m, l [rows, ns].
 // Partials of one workspace: o [rows, ns, 128], m, l [rows, ns]; split s of
 // the locator is column s0 + s.
 struct WsSplits {
