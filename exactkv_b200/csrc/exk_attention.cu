@@ -1482,6 +1482,7 @@ extern "C" int exk_attention_compressed(const uint16_t* q, const exk_cview* k, c
                                         void* stream) {
   if (ws == nullptr || out == nullptr) return EXK_EARG;
   if ((reinterpret_cast<uintptr_t>(out) & 7u) != 0) return EXK_EALIGN;
+  if (device_reachable(out) != 0) return EXK_EARG;
   int r = split_compressed(q, k, v, B, TS, Hkv, Hq, T, 0, ws->ns, ws, consumer_warps, qk_scale, status, device,
                            stream);
   return r != 0 ? r : launch_merge(ws, B * Hq, out, static_cast<cudaStream_t>(stream));
@@ -1493,6 +1494,7 @@ int devlen_args(const exk_partials* ws, const uint16_t* out, const int32_t* T_de
   if (ws == nullptr || out == nullptr || T_dev == nullptr || (T_stride != 0 && T_stride != 1)) return EXK_EARG;
   if (advance != 0 && T_stride != 0) return EXK_EARG;  // only a batch-wide length is advanced by the merge
   if ((reinterpret_cast<uintptr_t>(out) & 7u) != 0 || (reinterpret_cast<uintptr_t>(T_dev) & 3u) != 0) return EXK_EALIGN;
+  if (device_reachable(out) != 0) return EXK_EARG;
   const int last = (T_cap - 1) / (ws->split_len > 0 ? ws->split_len : 1);
   if (T_cap <= 0 || last + 1 != ws->ns) return EXK_EARG;  // the plan must be the capacity's
   return 0;
@@ -1528,6 +1530,7 @@ extern "C" int exk_attention_bf16(const uint16_t* q, const uint16_t* k, const ui
                                   float qk_scale, int32_t* status, int device, void* stream) {
   if (ws == nullptr || out == nullptr) return EXK_EARG;
   if ((reinterpret_cast<uintptr_t>(out) & 7u) != 0) return EXK_EALIGN;
+  if (device_reachable(out) != 0) return EXK_EARG;
   int r = split_bf16(q, k, v, B, TS, Hkv, Hq, T, 0, ws->ns, ws, consumer_warps, qk_scale, status, device, stream);
   return r != 0 ? r : launch_merge(ws, B * Hq, out, static_cast<cudaStream_t>(stream));
 }
@@ -1535,6 +1538,7 @@ extern "C" int exk_attention_bf16(const uint16_t* q, const uint16_t* k, const ui
 extern "C" int exk_attn_merge(const exk_partials* ws, int rows, uint16_t* out, int device, void* stream) {
   if (ws == nullptr || out == nullptr || rows <= 0 || ws->ns <= 0) return EXK_EARG;
   if (!aligned16(ws->o) || (reinterpret_cast<uintptr_t>(out) & 7u) != 0) return EXK_EALIGN;
+  if (device_reachable(out) != 0) return EXK_EARG;
   int r = use_device(device, nullptr);
   if (r != 0) return r;
   return launch_merge(ws, rows, out, static_cast<cudaStream_t>(stream));
@@ -1611,6 +1615,7 @@ extern "C" int exk_attn_merge_gathered(const float* buf, int world, const int32_
                                        uint16_t* out, int device, void* stream) {
   if (buf == nullptr || out == nullptr) return EXK_EARG;
   if (!aligned16(buf) || (reinterpret_cast<uintptr_t>(out) & 7u) != 0) return EXK_EALIGN;
+  if (device_reachable(out) != 0) return EXK_EARG;
   GatherArgs g = {};
   int r = gather_layout(g, world, counts, nmax, rows);
   if (r != 0) return r;
@@ -1624,6 +1629,7 @@ extern "C" int exk_attn_merge_peers(const float* const* blocks, int world, int r
                                     uint16_t* out, int32_t* status, int device, void* stream) {
   if (blocks == nullptr || out == nullptr || rank < 0 || rank >= world) return EXK_EARG;
   if ((reinterpret_cast<uintptr_t>(out) & 7u) != 0) return EXK_EALIGN;
+  if (device_reachable(out) != 0) return EXK_EARG;
   GatherArgs g = {};
   int r = gather_layout(g, world, counts, nmax, rows);
   if (r != 0) return r;

@@ -59,6 +59,17 @@ int use_device(int device, int* num_sms) {
   return 0;
 }
 
+int device_reachable(const void* p) {
+  cudaPointerAttributes at;
+  if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+    cudaGetLastError();  // clear the sticky-free error this call may leave
+    return EXK_EARG;
+  }
+  if (at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged) return 0;
+  if (at.type == cudaMemoryTypeHost && at.devicePointer == p) return 0;
+  return EXK_EARG;
+}
+
 }  // namespace exk
 
 extern "C" int exk_num_sms(int device) {

@@ -20,6 +20,11 @@ int use_device(int device, int* num_sms);
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// 0 if kernels may store through p: device or managed memory, or pinned host
+// memory mapped into the device address space at the same address (an output
+// written straight to the host over PCIe); EXK_EARG otherwise.
+int device_reachable(const void* p);
+
 inline int launch_status() {
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : static_cast<int>(e);

@@ -142,6 +142,16 @@ def _check_q(q, T, TS):
         raise ValueError(f"T={T} out of range (1..{TS})")
 
 
+def _check_out(out, q):
+    """An output for q's shape: a CUDA tensor, or pinned host memory that the merge
+    kernel writes directly (a zero-copy device-to-host result)."""
+    if out.shape != q.shape or out.dtype != torch.bfloat16 or not out.is_contiguous():
+        raise ValueError("out must be a contiguous bf16 tensor shaped like q")
+    if not out.is_cuda and not out.is_pinned():
+        raise ValueError("out must be a CUDA tensor or pinned host memory")
+    return out
+
+
 def attention_split(q, kc, vc, T, ws, s0, s1, num_warps=None):
     """Split partials of the compressed attention for splits [s0, s1) of ws's plan
     (the per-GPU step of a KV-sequence split). ws: (o, m, l, Partials)."""
@@ -297,7 +307,7 @@ def attention_compressed_devlen(q, kc, vc, T_dev, T_add=1, out=None, num_warps=N
     stream = torch.cuda.current_stream(q.device).cuda_stream
     ns, sl = plan_splits(B, Hkv, TS, dev)
     ws = _workspace(q.device, stream, B * Hq, ns, sl)
-    out = torch.empty_like(q) if out is None else out
+    out = torch.empty_like(q) if out is None else _check_out(out, q)
     rc = lib.exk_attention_compressed_devlen(q.data_ptr(), ctypes.byref(ka), ctypes.byref(va), B, TS, Hkv, Hq, TS,
                                              T_dev.data_ptr(), T_add, _stride_of(T_dev, B), advance,
                                              ctypes.byref(ws[3]), out.data_ptr(), _consumer_warps(num_warps),
@@ -318,7 +328,7 @@ def attention_reference_devlen(q, k, v, T_dev, T_add=0, out=None, num_warps=None
     stream = torch.cuda.current_stream(q.device).cuda_stream
     ns, sl = plan_splits(B, Hkv, TS, dev)
     ws = _workspace(q.device, stream, B * Hq, ns, sl)
-    out = torch.empty_like(q) if out is None else out
+    out = torch.empty_like(q) if out is None else _check_out(out, q)
     rc = lib.exk_attention_bf16_devlen(q.data_ptr(), k.data_ptr(), v.data_ptr(), B, TS, Hkv, Hq, TS, T_dev.data_ptr(),
                                        T_add, _stride_of(T_dev, B), 0, ctypes.byref(ws[3]), out.data_ptr(),
                                        _consumer_warps(num_warps), D ** -0.5 * LOG2E,

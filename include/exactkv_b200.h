@@ -8,6 +8,12 @@
  * caller owns every buffer, including the split-K workspace. Work is enqueued
  * on `stream` and nothing synchronises.
  *
+ * Outputs (`out` of the attention and merge entries) may also be pinned host
+ * memory mapped into the device's address space at the same address (any
+ * cudaHostAlloc / cudaHostRegister allocation under unified addressing): the
+ * merge kernel then writes the result straight to the host over PCIe, with no
+ * separate device-to-host copy. Other host memory is rejected (EXK_EARG).
+ *
  * Return value: 0 on success, a positive cudaError_t from the launch, or a
  * negative EXK_E* argument error (exk_error_string() describes every code).
  * Faults found by the kernels themselves (a spin-wait that ran out of time, a

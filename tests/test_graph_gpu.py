@@ -93,3 +93,37 @@ def test_graphed_steps_match_host_path():
     assert torch.equal(kernels.decode_to_bf16(kg.buffers(), kg.T), k[:, :kg.T])
     kernels.check_status()
     gs.close()
+
+
+def test_output_to_pinned_host_memory():
+    """The merge writes straight into pinned host memory (a zero-copy result, also
+    from a replayed graph): the same bits as a device output; pageable host
+    memory is refused before any launch."""
+    B, T, Hq, Hkv = 4, 1000, 32, 8
+    TS = 1024
+    k = synthetic.make_kv(B, TS, Hkv, seed=81, key=True)
+    v = synthetic.make_kv(B, TS, Hkv, seed=82, key=False)
+    q = synthetic.make_q(B, Hq, seed=83)
+    kc, vc = _pair(k, v, T, TS, 0.05)
+    lens = torch.full((1,), T, dtype=torch.int32, device="cuda")
+    ref = kernels.attention_compressed_devlen(q, kc, vc, lens, 0)
+    host = torch.empty(B, Hq, 128, dtype=torch.bfloat16).pin_memory()
+    kernels.attention_compressed_devlen(q, kc, vc, lens, 0, out=host)
+    torch.cuda.synchronize()
+    assert torch.equal(host.view(torch.int16), ref.cpu().view(torch.int16))
+    host.zero_()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        kernels.attention_compressed_devlen(q, kc, vc, lens, 0, out=host)   # warm the workspace on this stream
+        with torch.cuda.graph(g, stream=s):
+            kernels.attention_compressed_devlen(q, kc, vc, lens, 0, out=host)
+    host.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(host.view(torch.int16), ref.cpu().view(torch.int16))
+    del g
+    with pytest.raises(ValueError):
+        kernels.attention_compressed_devlen(q, kc, vc, lens, 0, out=torch.empty(B, Hq, 128, dtype=torch.bfloat16))
+    kernels.check_status()
