@@ -293,6 +293,145 @@ __global__ void __launch_bounds__(kEncWarps * 32) raw_copy_kernel(const __grid_c
   }
 }
 
+// Prefill launches (no device length) place raw rows in chunks of kChunkPh
+// page-heads instead of one CTA walking them all: chunk_sums_kernel writes each
+// chunk's raw-row count into the rowoff slot of the chunk's first page-head
+// (free until the final offsets: every rowoff of the launch is rewritten
+// below), chunk_scan_kernel (one CTA) turns those counts into offsets from the
+// pool counter and advances it, and chunk_place_kernel gives every page-head of
+// a chunk its offset and copies the chunk's raw rows. Same slots, same
+// (sequence, page, head) order as raw_offsets_kernel + raw_copy_kernel.
+constexpr int kChunkPh = 1024;
+constexpr int kChunkThreads = 256;  // four page-heads per thread
+
+__device__ __forceinline__ int64_t prefill_page(const EncArgs& a, int ph) {
+  int bi, pg, hk;
+  return page_index(a, a.pg0, ph, bi, pg, hk);
+}
+
+__global__ void __launch_bounds__(kChunkThreads) chunk_sums_kernel(const __grid_constant__ EncArgs a) {
+  __shared__ int s_warp[kChunkThreads / 32];
+  const int c0 = blockIdx.x * kChunkPh;
+  int n = 0;
+#pragma unroll
+  for (int j = 0; j < kChunkPh / kChunkThreads; ++j) {
+    const int ph = c0 + j * kChunkThreads + threadIdx.x;
+    if (ph < a.n_ph) n += __popc(static_cast<uint32_t>(a.rowmask[prefill_page(a, ph)]) & 0xFFFFu);
+  }
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) n += __shfl_xor_sync(0xFFFFFFFFu, n, d);
+  if ((threadIdx.x & 31) == 0) s_warp[threadIdx.x >> 5] = n;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int t = 0;
+    for (int w = 0; w < kChunkThreads / 32; ++w) t += s_warp[w];
+    a.rowoff[prefill_page(a, c0)] = t;
+  }
+}
+
+__global__ void __launch_bounds__(kScanThreads) chunk_scan_kernel(const __grid_constant__ EncArgs a) {
+  __shared__ int s_warp[kScanThreads / 32];
+  __shared__ int s_total;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int n_chunks = (a.n_ph + kChunkPh - 1) / kChunkPh;
+  int carry = *a.cnt;
+  for (int tile = 0; tile < n_chunks; tile += kScanThreads) {
+    const int c = tile + threadIdx.x;
+    const int64_t idx = c < n_chunks ? prefill_page(a, c * kChunkPh) : -1;
+    const int local = idx >= 0 ? a.rowoff[idx] : 0;
+    int incl = local;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int y = __shfl_up_sync(0xFFFFFFFFu, incl, d);
+      if (lane >= d) incl += y;
+    }
+    if (lane == 31) s_warp[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+      const int w = s_warp[lane];
+      int wi = w;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int y = __shfl_up_sync(0xFFFFFFFFu, wi, d);
+        if (lane >= d) wi += y;
+      }
+      s_warp[lane] = wi - w;
+      if (lane == 31) s_total = wi;
+    }
+    __syncthreads();
+    if (idx >= 0) a.rowoff[idx] = carry + s_warp[warp] + incl - local;
+    carry += s_total;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *a.cnt = carry;  // may exceed raw_cap: the caller grows the pool
+}
+
+template <bool VEC>
+__global__ void __launch_bounds__(kChunkThreads) chunk_place_kernel(const __grid_constant__ EncArgs a) {
+  __shared__ int s_off[kChunkPh];
+  __shared__ uint32_t s_rm[kChunkPh];
+  __shared__ int s_warp[kChunkThreads / 32];
+  __shared__ int s_base;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int c0 = blockIdx.x * kChunkPh;
+  constexpr int kPer = kChunkPh / kChunkThreads;
+  if (threadIdx.x == 0) s_base = a.rowoff[prefill_page(a, c0)];  // the chunk's offset, from chunk_scan_kernel
+  // counts of this thread's kPer consecutive page-heads
+  uint32_t rm[kPer];
+  int local = 0;
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int ph = c0 + threadIdx.x * kPer + j;
+    rm[j] = ph < a.n_ph ? static_cast<uint32_t>(a.rowmask[prefill_page(a, ph)]) & 0xFFFFu : 0u;
+    local += __popc(rm[j]);
+  }
+  int incl = local;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int y = __shfl_up_sync(0xFFFFFFFFu, incl, d);
+    if (lane >= d) incl += y;
+  }
+  if (lane == 31) s_warp[warp] = incl;
+  __syncthreads();
+  int wpre = 0;
+  for (int w = 0; w < warp; ++w) wpre += s_warp[w];
+  int off = s_base + wpre + incl - local;
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int i = threadIdx.x * kPer + j;
+    s_off[i] = off;
+    s_rm[i] = rm[j];
+    const int ph = c0 + i;
+    if (ph < a.n_ph) a.rowoff[prefill_page(a, ph)] = off;
+    off += __popc(rm[j]);
+  }
+  __syncthreads();
+  // each warp copies the raw rows of its share of the chunk, a row per step
+  for (int i = warp; i < kChunkPh; i += kChunkThreads / 32) {
+    uint32_t m = s_rm[i];
+    if (m == 0u) continue;
+    const int ph = c0 + i;
+    int bi, pg, hk;
+    page_index(a, a.pg0, ph, bi, pg, hk);
+    int64_t ridx = s_off[i];
+    while (m != 0u) {
+      const int tok = __ffs(m) - 1;
+      m &= m - 1u;
+      if (ridx >= 0 && ridx < a.raw_cap) {
+        const uint16_t* src = a.src + bi * a.s_b + pg * a.s_pg + static_cast<int64_t>(tok) * a.s_p + hk * a.s_h;
+        uint16_t* d = a.raw + ridx * kD;
+        if constexpr (VEC) {
+          reinterpret_cast<uint2*>(d)[lane] = reinterpret_cast<const uint2*>(src)[lane];
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) d[4 * lane + j] = src[4 * lane + j];
+        }
+      }
+      ++ridx;
+    }
+  }
+}
+
 struct DecArgs {
   const uint8_t* sm;
   const uint8_t* code;
@@ -409,12 +548,15 @@ extern "C" int exk_encode_pages(const uint16_t* src, int64_t s_b, int64_t s_pg, 
   else
     encode_kernel<false><<<blocks, kEncWarps * 32, 0, st>>>(a);
   if ((r = launch_status()) != 0) return r;
-  raw_offsets_kernel<<<1, kScanThreads, 0, st>>>(a);
+  const int chunks = static_cast<int>((n_ph + kChunkPh - 1) / kChunkPh);
+  chunk_sums_kernel<<<chunks, kChunkThreads, 0, st>>>(a);
+  if ((r = launch_status()) != 0) return r;
+  chunk_scan_kernel<<<1, kScanThreads, 0, st>>>(a);
   if ((r = launch_status()) != 0) return r;
   if (vec)
-    raw_copy_kernel<true><<<blocks, kEncWarps * 32, 0, st>>>(a);
+    chunk_place_kernel<true><<<chunks, kChunkThreads, 0, st>>>(a);
   else
-    raw_copy_kernel<false><<<blocks, kEncWarps * 32, 0, st>>>(a);
+    chunk_place_kernel<false><<<chunks, kChunkThreads, 0, st>>>(a);
   return launch_status();
 }
 
