@@ -81,9 +81,26 @@ __device__ __forceinline__ int64_t page_index(const EncArgs& a, int pg0, int ph,
   return (static_cast<int64_t>(a.b0 + bi) * a.NP + pg0 + pg) * a.H + hk;
 }
 
-__device__ __forceinline__ uint32_t half_of(const uint32_t (&w)[4], int c) {
-  // c 0..3: channels 4q+c (words 0,1); c 4..7: channels 64+4q+(c-4) (words 2,3)
-  return (w[c >> 1] >> (16 * (c & 1))) & 0xFFFFu;
+// Two 16-bit lanes per word (PTX integer SIMD; add wraps within each lane).
+__device__ __forceinline__ uint32_t max_u16x2(uint32_t x, uint32_t y) {
+  uint32_t d;
+  asm("max.u16x2 %0, %1, %2;" : "=r"(d) : "r"(x), "r"(y));
+  return d;
+}
+__device__ __forceinline__ uint32_t min_u16x2(uint32_t x, uint32_t y) {
+  uint32_t d;
+  asm("min.u16x2 %0, %1, %2;" : "=r"(d) : "r"(x), "r"(y));
+  return d;
+}
+__device__ __forceinline__ uint32_t max_s16x2(uint32_t x, uint32_t y) {
+  uint32_t d;
+  asm("max.s16x2 %0, %1, %2;" : "=r"(d) : "r"(x), "r"(y));
+  return d;
+}
+__device__ __forceinline__ uint32_t add_u16x2(uint32_t x, uint32_t y) {
+  uint32_t d;
+  asm("add.u16x2 %0, %1, %2;" : "=r"(d) : "r"(x), "r"(y));
+  return d;
 }
 
 template <bool VEC>
@@ -121,65 +138,79 @@ __global__ void __launch_bounds__(kEncWarps * 32, 4) encode_kernel(const __grid_
 
   // Two streaming passes over the lane's 8 rows (the second re-reads them from
   // L1): few registers, so four CTAs (32 warps) fit on an SM to hide latency.
-  // w: bf16 pairs (4q,4q+1), (4q+2,4q+3), (64+4q, ..), (64+4q+2, ..) of one row
+  // w: bf16 pairs (4q,4q+1), (4q+2,4q+3), (64+4q, ..), (64+4q+2, ..) of one row.
+  // Both passes work on two values at once in 16-bit lanes (exponents are 8
+  // bits, codes and their differences fit a signed 16-bit lane).
   const uint16_t* rows = a.src + bi * a.s_b + pg * a.s_pg + static_cast<int64_t>(th * 8) * a.s_p + hk * a.s_h;
-  // pass 1: per-channel maximum exponent and zero presence over the 16 tokens
-  int emax[8];
-  uint32_t has0 = 0;
+  // pass 1: per-channel maximum and minimum exponent over the 16 tokens
+  uint32_t emax2[4], emin2[4];
 #pragma unroll
-  for (int c = 0; c < 8; ++c) emax[c] = 0;
+  for (int j = 0; j < 4; ++j) {
+    emax2[j] = 0u;
+    emin2[j] = 0xFFFFFFFFu;
+  }
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     uint32_t w[4];
     load_row_quads<VEC>(rows + static_cast<int64_t>(i) * a.s_p, q, w);
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      const int e = (half_of(w, c) >> 7) & 0xFF;
-      emax[c] = max(emax[c], e);
-      has0 |= (e == 0 ? 1u : 0u) << c;
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t e2 = (w[j] >> 7) & 0x00FF00FFu;
+      emax2[j] = max_u16x2(emax2[j], e2);
+      emin2[j] = min_u16x2(emin2[j], e2);
     }
   }
 #pragma unroll
-  for (int c = 0; c < 8; ++c) emax[c] = max(emax[c], __shfl_xor_sync(0xFFFFFFFFu, emax[c], 16));
-  has0 |= __shfl_xor_sync(0xFFFFFFFFu, has0, 16);
-
-  int bse[8];
-  bool zm[8];
-  uint32_t bw[2] = {0u, 0u};
-#pragma unroll
-  for (int c = 0; c < 8; ++c) {
-    bse[c] = max(emax[c] - 15, 0);
-    zm[c] = ((has0 >> c) & 1u) && bse[c] > 0;  // a zero the plain 15-step window cannot hold
-    const int byte = min(zm[c] ? bse[c] + 128 : bse[c], 255);
-    bw[c >> 2] |= uint32_t(byte) << (8 * (c & 3));
+  for (int j = 0; j < 4; ++j) {
+    emax2[j] = max_u16x2(emax2[j], __shfl_xor_sync(0xFFFFFFFFu, emax2[j], 16));
+    emin2[j] = min_u16x2(emin2[j], __shfl_xor_sync(0xFFFFFFFFu, emin2[j], 16));
   }
 
-  // pass 2: codes, sign|mantissa bytes and escapes, row by row
-  uint32_t escrow = 0;
+  // per channel: base b = max(emax - 15, 0); zero group zm = (a zero exponent
+  // and b > 0); then, as 16-bit lane pairs, -b and -(b + zm) for pass 2
+  uint32_t bw[2] = {0u, 0u}, nb2[4] = {0u, 0u, 0u, 0u}, nbz2[4] = {0u, 0u, 0u, 0u};
+  bool escall = false;
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    const int sh = 16 * (c & 1);
+    const int emax = static_cast<int>((emax2[c >> 1] >> sh) & 0xFFFFu);
+    const bool has0 = ((emin2[c >> 1] >> sh) & 0xFFFFu) == 0u;
+    const int bse = max(emax - 15, 0);
+    const bool zm = has0 && bse > 0;  // a zero the plain 15-step window cannot hold
+    const int byte = min(zm ? bse + 128 : bse, 255);
+    bw[c >> 2] |= uint32_t(byte) << (8 * (c & 3));
+    nb2[c >> 1] |= (static_cast<uint32_t>(-bse) & 0xFFFFu) << sh;
+    nbz2[c >> 1] |= (static_cast<uint32_t>(-(bse + (zm ? 1 : 0))) & 0xFFFFu) << sh;
+    escall |= bse >= 128;
+  }
+
+  // pass 2: codes, sign|mantissa bytes and escapes, row by row. Per value:
+  // code = max(e - b, 0) (a zero of a zero group gets 0); it escapes when
+  // e != 0 and e < b + zm, or when b >= 128.
+  uint32_t escrow = escall ? 0xFFu : 0u;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int tok = th * 8 + i;
     const int64_t row = (static_cast<int64_t>(a.b0 + bi) * a.TS + (pg0 + pg) * kP + tok) * a.H + hk;
     uint32_t w[4];
     load_row_quads<VEC>(rows + static_cast<int64_t>(i) * a.s_p, q, w);
-    uint32_t smw[2] = {0u, 0u}, cw = 0u;
-    bool esc = false;
+    uint32_t code2[4], x[4], escacc = 0u;
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      const uint32_t u = half_of(w, c);
-      const int e = (u >> 7) & 0xFF;
-      const bool zero = zm[c] && e == 0;
-      int code = zero ? 0 : e - bse[c];
-      const int lo = zm[c] ? 1 : 0;
-      esc |= (code < lo && !zero) || bse[c] >= 128;
-      code = min(max(code, 0), 15);
-      smw[c >> 2] |= (((u >> 8) & 0x80u) | (u & 0x7Fu)) << (8 * (c & 3));
-      cw |= uint32_t(code) << (8 * (c & 3) + 4 * (c >> 2));
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t e2 = (w[j] >> 7) & 0x00FF00FFu;
+      code2[j] = max_s16x2(add_u16x2(e2, nb2[j]), 0u);
+      // lane bit 15: e < b + zm; e2 + 0x7FFF: lane bit 15 iff e != 0
+      escacc |= add_u16x2(e2, nbz2[j]) & (e2 + 0x7FFF7FFFu);
+      // sign to bit 7 of the low byte of each lane, beside the mantissa
+      const uint32_t t = w[j] & 0x807F807Fu;
+      x[j] = t | (t >> 8);
     }
-    *reinterpret_cast<uint32_t*>(a.sm + row * kD + 4 * q) = smw[0];
-    *reinterpret_cast<uint32_t*>(a.sm + row * kD + 64 + 4 * q) = smw[1];
+    const uint32_t smw0 = prmt(x[0], x[1], 0x6420u), smw1 = prmt(x[2], x[3], 0x6420u);
+    const uint32_t cw = prmt(code2[0], code2[1], 0x6420u) | (prmt(code2[2], code2[3], 0x6420u) << 4);
+    *reinterpret_cast<uint32_t*>(a.sm + row * kD + 4 * q) = smw0;
+    *reinterpret_cast<uint32_t*>(a.sm + row * kD + 64 + 4 * q) = smw1;
     *reinterpret_cast<uint32_t*>(a.code + row * (kD / 2) + 4 * q) = cw;
-    escrow |= (esc ? 1u : 0u) << i;
+    escrow |= ((escacc & 0x80008000u) != 0u ? 1u : 0u) << i;
   }
   if (th == 0) {
     *reinterpret_cast<uint32_t*>(a.base + page * kD + 4 * q) = bw[0];
