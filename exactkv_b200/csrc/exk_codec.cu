@@ -81,6 +81,22 @@ __device__ __forceinline__ int64_t page_index(const EncArgs& a, int pg0, int ph,
   return (static_cast<int64_t>(a.b0 + bi) * a.NP + pg0 + pg) * a.H + hk;
 }
 
+// Constants the compiler cannot see (2^25, 2^24, 1), so that the shifts and one
+// add of the encoder's second pass become multiplies on the FMA pipe: that
+// pass keeps the ALU pipe busy.
+static __constant__ uint32_t c_fma[3] = {1u << 25, 1u << 24, 1u};
+
+__device__ __forceinline__ uint32_t mulhi(uint32_t x, uint32_t k) {
+  uint32_t d;
+  asm("mul.hi.u32 %0, %1, %2;" : "=r"(d) : "r"(x), "r"(k));
+  return d;
+}
+__device__ __forceinline__ uint32_t mad_lo(uint32_t x, uint32_t k, uint32_t y) {
+  uint32_t d;
+  asm("mad.lo.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(x), "r"(k), "r"(y));
+  return d;
+}
+
 // Two 16-bit lanes per word (PTX integer SIMD; add wraps within each lane).
 __device__ __forceinline__ uint32_t max_u16x2(uint32_t x, uint32_t y) {
   uint32_t d;
@@ -155,7 +171,7 @@ __global__ void __launch_bounds__(kEncWarps * 32, 4) encode_kernel(const __grid_
     load_row_quads<VEC>(rows + static_cast<int64_t>(i) * a.s_p, q, w);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const uint32_t e2 = (w[j] >> 7) & 0x00FF00FFu;
+      const uint32_t e2 = w[j] & 0x7F807F80u;  // exponents, 7 bits up in their lanes
       emax2[j] = max_u16x2(emax2[j], e2);
       emin2[j] = min_u16x2(emin2[j], e2);
     }
@@ -173,7 +189,7 @@ __global__ void __launch_bounds__(kEncWarps * 32, 4) encode_kernel(const __grid_
 #pragma unroll
   for (int c = 0; c < 8; ++c) {
     const int sh = 16 * (c & 1);
-    const int emax = static_cast<int>((emax2[c >> 1] >> sh) & 0xFFFFu);
+    const int emax = static_cast<int>((emax2[c >> 1] >> (sh + 7)) & 0xFFu);
     const bool has0 = ((emin2[c >> 1] >> sh) & 0xFFFFu) == 0u;
     const int bse = max(emax - 15, 0);
     const bool zm = has0 && bse > 0;  // a zero the plain 15-step window cannot hold
@@ -188,6 +204,7 @@ __global__ void __launch_bounds__(kEncWarps * 32, 4) encode_kernel(const __grid_
   // code = max(e - b, 0) (a zero of a zero group gets 0); it escapes when
   // e != 0 and e < b + zm, or when b >= 128.
   uint32_t escrow = escall ? 0xFFu : 0u;
+  const uint32_t k25 = c_fma[0], k24 = c_fma[1], k1 = c_fma[2];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int tok = th * 8 + i;
@@ -197,13 +214,13 @@ __global__ void __launch_bounds__(kEncWarps * 32, 4) encode_kernel(const __grid_
     uint32_t code2[4], x[4], escacc = 0u;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const uint32_t e2 = (w[j] >> 7) & 0x00FF00FFu;
+      const uint32_t e2 = mulhi(w[j], k25) & 0x00FF00FFu;  // (w >> 7): exponents in the low byte of each lane
       code2[j] = max_s16x2(add_u16x2(e2, nb2[j]), 0u);
       // lane bit 15: e < b + zm; e2 + 0x7FFF: lane bit 15 iff e != 0
-      escacc |= add_u16x2(e2, nbz2[j]) & (e2 + 0x7FFF7FFFu);
-      // sign to bit 7 of the low byte of each lane, beside the mantissa
-      const uint32_t t = w[j] & 0x807F807Fu;
-      x[j] = t | (t >> 8);
+      escacc |= add_u16x2(e2, nbz2[j]) & mad_lo(e2, k1, 0x7FFF7FFFu);
+      // bit 7 of each lane's low byte from the sign (w >> 8), bits 0-6 the
+      // mantissa; the high bytes are not used
+      x[j] = (mulhi(w[j], k24) & 0x00800080u) | (w[j] & 0xFF7FFF7Fu);
     }
     const uint32_t smw0 = prmt(x[0], x[1], 0x6420u), smw1 = prmt(x[2], x[3], 0x6420u);
     const uint32_t cw = prmt(code2[0], code2[1], 0x6420u) | (prmt(code2[2], code2[3], 0x6420u) << 4);
@@ -332,8 +349,8 @@ __global__ void __launch_bounds__(kEncWarps * 32) raw_copy_kernel(const __grid_c
 // pool counter and advances it, and chunk_place_kernel gives every page-head of
 // a chunk its offset and copies the chunk's raw rows. Same slots, same
 // (sequence, page, head) order as raw_offsets_kernel + raw_copy_kernel.
-constexpr int kChunkPh = 1024;
-constexpr int kChunkThreads = 256;  // four page-heads per thread
+constexpr int kChunkPh = 256;
+constexpr int kChunkThreads = 256;  // one page-head per thread
 
 __device__ __forceinline__ int64_t prefill_page(const EncArgs& a, int ph) {
   int bi, pg, hk;
