@@ -443,7 +443,7 @@ def time_encoder(kbf, B, T, Hkv, dev, reps=5):
     written = rows * 192 + (rows // 16) * 136 + n * 256
     return {"us": round(us, 2), "bf16_read_gbs": round(rows * 256 / us / 1e3, 1),
             "compressed_written_gbs": round(written / us / 1e3, 1), "raw_rows": n,
-            "what": f"encode_pages over {B} x {T} tokens x {Hkv} heads of keys (3 launches: encode, slot scan, raw copy)"}
+            "what": f"encode_pages over {B} x {T} tokens x {Hkv} heads of keys (4 launches: encode, chunk sums, chunk scan, slot placement + raw copy)"}
 
 
 def run_e2e(a, kc, vc, B, Hq, Hkv, T0, dev, world, raw_rows0, ns0):

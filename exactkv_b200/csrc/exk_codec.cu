@@ -5,11 +5,12 @@
 // 64+4q..64+4q+3 of tokens 8th..8th+7, so a channel's 16 exponents live in
 // lanes q and q+16 and one shuffle completes every per-channel reduction.
 // Raw-pool slots are assigned in (sequence, page, head) order — the order the
-// reference's encode_reference writes them (exactkv/codec.py:49-53) — in three
+// reference's encode_reference writes them (exactkv/codec.py:49-53) — by
 // launches that never wait on one another: encode_kernel writes sm, code, base
-// and rowmask; raw_offsets_kernel (one CTA) scans the pages' raw-row counts
-// from the pool counter, writes rowoff and advances the counter;
-// raw_copy_kernel copies every escaped row from the source into its slot.
+// and rowmask; then for a prefill, chunk_sums / chunk_scan / chunk_place
+// (below) turn the pages' raw-row counts into rowoff from the pool counter,
+// advance it and copy every escaped row into its slot; for a one-token append,
+// raw_offsets_kernel (one CTA) scans the page-heads and raw_copy_kernel copies.
 // The reference takes a slot range with one atomic_add per page-head
 // (exactkv/kernels.py:261-268), whose order depends on scheduling.
 #include <algorithm>

@@ -204,7 +204,8 @@ int exk_attention_bf16(const uint16_t *q, const uint16_t *k, const uint16_t *v,
  * pool slots cnt, cnt+1, ... in (sequence, page, head) order — the order of
  * the reference's encode_reference; `cnt` advances even past raw_cap, but
  * slots at or past raw_cap are not written (the caller grows the pool and
- * encodes again). Three launches on `stream` (encode, slot scan, raw copy).
+ * encodes again). Four launches on `stream` (encode, chunk sums, chunk scan,
+ * slot placement + raw copy).
  * Replaces _encode_pages_kernel/encode_pages (exactkv/kernels.py:233-268, 340-346). */
 int exk_encode_pages(const uint16_t *src, int64_t s_b, int64_t s_pg, int64_t s_p, int64_t s_h,
                      uint8_t *sm, uint8_t *code, uint8_t *base, int32_t *rowmask, int32_t *rowoff,
