@@ -184,8 +184,11 @@ def attention_split_bf16(q, k, v, T, ws, s0, s1, num_warps=None):
 
 
 def merge_partials(ws, rows, out):
-    stream = torch.cuda.current_stream(out.device).cuda_stream
-    check(lib.exk_attn_merge(ctypes.byref(ws[3]), rows, out.data_ptr(), out.device.index, stream), "exk_attn_merge")
+    """Merge of the workspace's splits into bf16 out [rows, 128] (a CUDA tensor or
+    pinned host memory), on the workspace device's current stream."""
+    dev = ws[0].device
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    check(lib.exk_attn_merge(ctypes.byref(ws[3]), rows, out.data_ptr(), dev.index, stream), "exk_attn_merge")
     return out
 
 

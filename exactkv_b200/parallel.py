@@ -189,9 +189,9 @@ def merge_gathered(gathered, plan, out):
     if gathered.shape != (plan.world, block_floats(rows)):
         raise ValueError("gathered blocks do not match the plan")
     counts = (ctypes.c_int32 * plan.world)(*plan.group_counts)
-    stream = torch.cuda.current_stream(out.device).cuda_stream
+    stream = torch.cuda.current_stream(gathered.device).cuda_stream
     check(lib.exk_attn_merge_gathered(gathered.data_ptr(), plan.world, counts, 1, rows, out.data_ptr(),
-                                      out.device.index, stream), "exk_attn_merge_gathered")
+                                      gathered.device.index, stream), "exk_attn_merge_gathered")
     return out
 
 
@@ -207,7 +207,7 @@ def merge_two_level(ws, plan, rows, out):
     split of the plan: each rank's run reduced to its group partial, then the
     groups merged in rank order — the same bits as the plan run on plan.world
     GPUs."""
-    gathered = torch.empty(plan.world, block_floats(rows), dtype=torch.float32, device=out.device)
+    gathered = torch.empty(plan.world, block_floats(rows), dtype=torch.float32, device=ws[0].device)
     for r in range(plan.world):
         n = plan.count(r)
         if n:
@@ -237,8 +237,8 @@ def merge_peers(blocks, plan, rank, flags, peer_flags, epoch, out):
     peer_flags[p] word `rank` of peer p's flags (PeerExchange builds these from
     symmetric memory)."""
     w = plan.world
-    dev = out.device.index
-    stream = torch.cuda.current_stream(out.device).cuda_stream
+    dev = torch.cuda.current_device() if not out.is_cuda else out.device.index
+    stream = torch.cuda.current_stream(dev).cuda_stream
     check(lib.exk_attn_merge_peers((ctypes.c_void_p * w)(*blocks), w, rank, (ctypes.c_int32 * w)(*plan.group_counts),
                                    1, out.shape[0] * out.shape[1], flags, (ctypes.c_void_p * w)(*peer_flags), epoch,
                                    out.data_ptr(), kernels.status_tensor(dev).data_ptr(), dev, stream),
@@ -312,8 +312,8 @@ class PeerExchange:
     def merge(self, out):
         """Second half: signal the peers, wait for theirs, merge every rank's group
         partial of this epoch into bf16 out [B, Hq, 128]."""
-        dev = out.device.index
-        stream = torch.cuda.current_stream(out.device).cuda_stream
+        dev = self.device.index
+        stream = torch.cuda.current_stream(self.device).cuda_stream
         check(lib.exk_attn_merge_peers(self._blocks[self.epoch & 1], self.world, self.rank, self._counts, 1,
                                        self.rows, self._flags, self._peer_flags, self.epoch & 0xFFFFFFFF,
                                        out.data_ptr(), kernels.status_tensor(dev).data_ptr(), dev, stream),
