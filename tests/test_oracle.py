@@ -77,3 +77,35 @@ def test_bf16_conversion_rne():
     assert np.array_equal(bits_to_f32(f32_to_bits(x)), np.array([1.0, 1.0, 1.015625, -2.5, np.inf, -np.inf, 0.0, -0.0],
                                                                   np.float32))
     assert np.isnan(bits_to_f32(f32_to_bits(np.array([np.nan], np.float32))))[0]
+
+
+@pytest.mark.parametrize("case", CONFIG1, ids=lambda c: c["name"])
+def test_oracle_two_level_merge(case):
+    """The KV-sequence split's two-level merge (oracle.attention.merge_group per run
+    of splits, then merge over the runs) against the float64 attention, with the
+    same tolerance as the one-level merge; a run of one split is that split's
+    partial unchanged, and empty splits (m = -inf) weigh nothing."""
+    q, k, v = config1_inputs(case)
+    T = case["T"]
+    B, Hq, D = q.shape
+    ns = 7
+    per = -(-T // ns)
+    sl = -(-per // 16) * 16              # ns splits of whole pages covering T
+    o, m, l = oatt.split_partials(q, k, v, T, splits=(ns, sl))
+    rows = B * Hq
+    o, m, l = o.reshape(rows, ns, D), m.reshape(rows, ns), l.reshape(rows, ns)
+    for bounds in ([0, 3, 7], [0, 1, 2, 4, 7], [0, 7]):
+        groups = [oatt.merge_group(o[:, a:b], m[:, a:b], l[:, a:b]) for a, b in zip(bounds, bounds[1:])]
+        go = np.stack([g[0] for g in groups], 1)
+        gm = np.stack([g[1] for g in groups], 1)
+        gl = np.stack([g[2] for g in groups], 1)
+        out = bits_to_f32(f32_to_bits(oatt.merge(go, gm, gl))).reshape(B, Hq, D).astype(np.float64)
+        ref = oatt.attention_f64(q, k, v, T)
+        assert (np.abs(out - ref) <= oatt.tolerance(q, k, v, T, ref)).all(), bounds
+    g1 = oatt.merge_group(o[:, 2:3], m[:, 2:3], l[:, 2:3])
+    assert np.array_equal(g1[0], o[:, 2]) and np.array_equal(g1[1], m[:, 2]) and np.array_equal(g1[2], l[:, 2])
+    m2 = m.copy()
+    m2[:, 5] = -np.inf
+    ge = oatt.merge_group(np.where(np.isneginf(m2)[..., None], 0, o), m2, np.where(np.isneginf(m2), 0, l))
+    gd = oatt.merge_group(np.delete(o, 5, 1), np.delete(m, 5, 1), np.delete(l, 5, 1))
+    assert all(np.array_equal(a, b) for a, b in zip(ge, gd))
