@@ -75,3 +75,40 @@ def test_plan_rejects_bad_arguments():
     ns, sl = ctypes.c_int32(), ctypes.c_int32()
     assert lib.exk_plan_splits(0, 8, 4096, 148, ctypes.byref(ns), ctypes.byref(sl)) == -1
     assert lib.exk_plan_splits(1, 8, 0, 148, ctypes.byref(ns), ctypes.byref(sl)) == -1
+
+
+def test_entry_points_reject_bad_arguments_before_any_launch():
+    """Argument errors come back as negative codes from the host-side checks that
+    run before any CUDA call (fake, never dereferenced device addresses)."""
+    from exactkv_b200._lib import lib, CView, Partials
+    EARG, EALIGN, EHEADS = -1, -2, -5
+    dev_addr = 1 << 40                     # 16-byte aligned, never touched
+    ws = Partials(dev_addr, dev_addr + (1 << 20), dev_addr + (2 << 20), 4, 64, 0)
+    cv = CView(dev_addr, dev_addr, dev_addr, dev_addr, dev_addr, dev_addr, 1024)
+    st = ctypes.c_void_p(0)
+
+    def split(q=dev_addr, k=cv, B=1, TS=256, Hkv=8, Hq=32, T=200, s0=0, s1=4, w=ws, nwc=8):
+        return lib.exk_attn_split_compressed(q, ctypes.byref(k) if k is not None else None,
+                                             ctypes.byref(cv), B, TS, Hkv, Hq, T, s0, s1,
+                                             ctypes.byref(w) if w is not None else None, nwc, 0.1, st, 0, None)
+
+    assert split(k=None) == EARG                       # null cache view
+    assert split(w=None) == EARG                       # no workspace
+    assert split(Hkv=1, Hq=32) == EHEADS               # 32 query heads per KV head
+    assert split(Hq=30) == EARG                        # Hq not a multiple of Hkv
+    assert split(nwc=6) == EARG                        # 4, 8 consumer warps only
+    assert split(T=300) == EARG                        # T past the capacity TS
+    assert split(s0=3, s1=3) == EARG                   # empty split range
+    assert split(q=dev_addr + 8) == EALIGN             # q not 16-byte aligned
+    short = Partials(dev_addr, dev_addr, dev_addr, 2, 64, 0)
+    assert split(w=short, s1=2) == EARG                # the plan does not cover T
+    bad_heads = Partials(dev_addr, dev_addr, dev_addr, 4, 64, 3)
+    assert split(w=bad_heads) == EARG                  # heads per item must be 1, 2, 4 or 8
+    counts = (ctypes.c_int32 * 2)(1, 1)
+    flags = (ctypes.c_void_p * 2)(dev_addr, dev_addr)
+    assert lib.exk_attn_merge_peers(flags, 2, 2, counts, 1, 32, dev_addr, flags, 1, dev_addr, None, 0, None) == EARG
+    assert lib.exk_attn_merge_partial(ctypes.byref(ws), 32, 3, 3, dev_addr, dev_addr, dev_addr, 0, None) == EARG
+    assert lib.exk_attn_merge_partial(ctypes.byref(ws), 32, 0, 5, dev_addr, dev_addr, dev_addr, 0, None) == EARG
+    for code in (EARG, EALIGN, -3, -4, EHEADS, -6):
+        assert lib.exk_error_string(code).startswith(b"exactkv_b200:")
+    assert b"peer" in lib.exk_status_string(6)
