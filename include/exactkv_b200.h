@@ -117,7 +117,10 @@ int exk_attn_split_bf16(const uint16_t *q, const uint16_t *k, const uint16_t *v,
 
 /* Merge of the split partials into bf16 out [rows, 128]:
  * out = sum_s o_s 2^(m_s - M) / sum_s l_s 2^(m_s - M), M = max_s m_s.
- * Replaces _reduce_kernel (exactkv/kernels.py:33-43). */
+ * Up to 16 splits: one warp per row, sums in split order. More: one CTA per
+ * row, each warp folding chunks of 8 splits with its running maximum, the
+ * warps combined in order; the order depends only on ns, so merges of the same
+ * splits agree bit for bit. Replaces _reduce_kernel (exactkv/kernels.py:33-43). */
 int exk_attn_merge(const exk_partials *ws, int rows, uint16_t *out, int device, void *stream);
 
 /* Splits [s0, s1) of `ws` merged into one partial per row, the partial of the
