@@ -141,6 +141,14 @@ __device__ __forceinline__ int valid_tokens(const AttnArgs& a, int b) {
 
 // An item whose split lies past its sequence's length has no pages: its warps
 // write an empty partial (m = -inf, l = 0, o = 0), which the merge weighs with 0.
+// With device lengths the plan fixes only the number of splits: sequence b's
+// splits are runs of ceil(ceil(T_b / 16) / ns) pages, so the work stays
+// balanced however far the cache is from the capacity the plan was made for.
+__device__ __forceinline__ int item_split_len(const AttnArgs& a, int T) {
+  if (a.T_dev == nullptr) return a.split_len;
+  return max(1, ((T + kP - 1) / kP + a.ns - 1) / a.ns) * kP;
+}
+
 __device__ __forceinline__ Item decode_item(const AttnArgs& a, int item) {
   Item it;
   const int bg = item / a.nsl;
@@ -148,8 +156,9 @@ __device__ __forceinline__ Item decode_item(const AttnArgs& a, int item) {
   it.b = bg / a.ngroups;
   it.hg = bg % a.ngroups;
   const int T = valid_tokens(a, it.b);
-  it.tok0 = it.split * a.split_len;
-  it.tok1 = max(it.tok0, min(it.tok0 + a.split_len, T));
+  const int sl = item_split_len(a, T);
+  it.tok0 = it.split * sl;
+  it.tok1 = max(it.tok0, min(it.tok0 + sl, T));
   it.page0 = it.tok0 / kP;
   it.npages = (it.tok1 - it.tok0 + kP - 1) / kP;
   return it;

@@ -300,7 +300,8 @@ def advance_length(T_dev, n=1):
 def attention_compressed_devlen(q, kc, vc, T_dev, T_add=1, out=None, num_warps=None, advance=0):
     """Decode attention over the first min(TS, T_dev + T_add) tokens of the caches
     (T_dev: one int32 length for the batch or one per sequence), with the split
-    plan for their capacity TS (see exk_attention_compressed_devlen); advance != 0
+    plan's number of splits for their capacity TS, each sequence cut into that many
+    equal page runs of its current length (see exk_attention_compressed_devlen); advance != 0
     then adds it to the batch length on the device (the end of a step)."""
     ka, TS, Hkv = _cache_args(kc)
     va, _, _ = _cache_args(vc)

@@ -176,8 +176,11 @@ int exk_attention_compressed(const uint16_t *q, const exk_cview *k, const exk_cv
  * length for the batch; 1: one per sequence, a variable-length batch), so one
  * enqueued call (e.g. inside a captured CUDA graph) serves every step of a
  * growing cache. `ws` must hold the plan for T_cap (its splits exactly cover
- * T_cap); splits past T_b contribute nothing. Same results as
- * exk_attention_compressed with that plan at length T_b. With advance != 0
+ * T_cap); of that plan the kernel keeps the number of splits ns and cuts
+ * sequence b into ns runs of ceil(ceil(T_b / 16) / ns) pages, so the work
+ * stays balanced at any length (runs past T_b are empty and weigh nothing).
+ * Same results as exk_attention_compressed with ns splits of that length at
+ * length T_b (ns <= 256). With advance != 0
  * (T_stride 0 only) the merge then adds `advance` to *T_dev (the end of a
  * step). No counterpart in the reference (its calls take one host-side T). */
 int exk_attention_compressed_devlen(const uint16_t *q, const exk_cview *k, const exk_cview *v,

@@ -27,8 +27,11 @@ def _pair(k, v, T0, TS, reserve):
     return kc, vc
 
 
-def _host_attention(q, kc, vc, T, ns_cap, sl):
-    """The plan for the capacity, run over the splits that hold tokens."""
+def _host_attention(q, kc, vc, T, ns_cap):
+    """What the device-length call computes: the capacity plan's number of splits,
+    each ceil(ceil(T / 16) / ns_cap) pages long, run over the splits that hold
+    tokens."""
+    sl = -(-(-(-T // 16)) // ns_cap) * 16
     n = -(-T // sl)
     B, Hq, _ = q.shape
     o = torch.empty(B * Hq, n, 128, device="cuda")
@@ -46,7 +49,7 @@ def test_graphed_steps_match_host_path():
     qs = torch.stack([synthetic.make_q(B, Hq, seed=100 + i) for i in range(steps)])
     ka, va = _pair(k, v, T0, TS, reserve=1.0)
     kg, vg = _pair(k, v, T0, TS, reserve=0.002)
-    ns, sl = kernels.plan_splits(B, Hkv, TS)
+    ns, _ = kernels.plan_splits(B, Hkv, TS)
     ekv.decode_attention(qs[0], kg, vg)          # configures the kernels before any capture
 
     length = DeviceLength([kg, vg])
@@ -75,7 +78,7 @@ def test_graphed_steps_match_host_path():
         va.append(v[:, t])
         if ka.T % 16 == 0:
             ekv.check_overflow([ka, va])
-        ref = _host_attention(qs[i], ka, va, ka.T, ns, sl)
+        ref = _host_attention(qs[i], ka, va, ka.T, ns)
         assert torch.equal(out.view(torch.int16), ref.view(torch.int16)), i
     torch.cuda.synchronize()
     assert gs.captures >= 2 and kg.grows + vg.grows > grows
