@@ -51,6 +51,23 @@ def test_plan_partition_covers_every_split_once():
         KVSplitPlan(1, 8, 4096, 2, 4, 464)     # splits do not cover T
 
 
+def test_plan_head_groups_for_short_items(monkeypatch):
+    """KVSplitPlan.make keeps the default head group while items hold >= 24 pages
+    and halves it (down to 2) otherwise; every rank's items still fit one wave
+    of its SMs and the splits cover the sequence."""
+    from exactkv_b200 import kernels
+    monkeypatch.setattr(kernels, "num_sms", lambda device=None: 148)
+    for world, heads in [(1, 0), (2, 0), (4, 4), (8, 2)]:
+        plan = KVSplitPlan.make(1, 8, 131072, world)
+        assert plan.heads == heads, world
+        assert plan.ns * plan.split_len >= 131072 and plan.split_len % 16 == 0
+        units = 8 // (plan.heads or 8)
+        assert all(units * n <= 148 for n in plan.counts), (world, plan.counts)
+        if plan.heads:
+            assert plan.split_len // 16 >= KVSplitPlan.MIN_ITEM_PAGES
+            assert (plan.split_len // 16) % (8 // plan.heads) == 0   # whole stages per warp
+
+
 def _oracle_block(qb, kb, vb, plan, rank):
     """One rank's flat block: the group partial of its splits, by the oracle over
     the rank's tokens only."""
