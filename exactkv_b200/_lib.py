@@ -38,6 +38,12 @@ _SIGNATURES.update({
     "exk_attn_split_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                                     _P(Partials), c_int, c_float, c_void_p, c_int, c_void_p]),
     "exk_attn_merge": (c_int, [_P(Partials), c_int, c_void_p, c_int, c_void_p]),
+    "exk_attention_compressed_paged": (c_int, [c_void_p, _P(CView), _P(CView), c_int, c_int, c_int, c_int, c_void_p,
+                                               c_int, c_void_p, _P(Partials), c_void_p, c_int, c_float, c_void_p,
+                                               c_int, c_void_p]),
+    "exk_attention_bf16_paged": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int,
+                                         c_void_p, _P(Partials), c_void_p, c_int, c_float, c_void_p, c_int,
+                                         c_void_p]),
     "exk_attn_merge_partial": (c_int, [_P(Partials), c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int,
                                        c_void_p]),
     "exk_attn_merge_gathered": (c_int, [c_void_p, c_int, _P(c_int32), c_int, c_int, c_void_p, c_int, c_void_p]),

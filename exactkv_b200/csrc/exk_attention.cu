@@ -58,6 +58,11 @@ struct AttnArgs {
   int T_add, T_stride;          // (T is then the capacity; T_stride 0: one length for the batch)
   int ns, split_len, s0, nsl, n_items, ngroups;
   float qk_scale;
+  // Paged caches: page pg of sequence b is page pages[b * pages_stride + pg] of
+  // a pool of pool_pages pages (the cache buffers seen as [pool_pages, 16, H,
+  // *]); nullptr: page b * NP + pg of the [B, TS] buffers.
+  const int32_t* pages;
+  int pages_stride, pool_pages;
 };
 
 // Compressed: ksm, kcode, kbase, vsm, vcode, vbase.  bf16: k, v.
@@ -144,6 +149,20 @@ __device__ __forceinline__ int valid_tokens(const AttnArgs& a, int b) {
 // With device lengths the plan fixes only the number of splits: sequence b's
 // splits are runs of ceil(ceil(T_b / 16) / ns) pages, so the work stays
 // balanced however far the cache is from the capacity the plan was made for.
+// The cache page holding page pg of sequence b; -1 when a block-table entry is
+// outside the pool (nothing of it is read: its TMA boxes start at a negative
+// row and fill with zeros, and the metadata is skipped; the status word gets
+// EXK_S_PAGE_INDEX).
+__device__ __forceinline__ int page_of(const AttnArgs& a, int b, int pg) {
+  if (a.pages == nullptr) return b * a.NP + pg;
+  const int p = __ldg(a.pages + static_cast<int64_t>(b) * a.pages_stride + pg);
+  if (p < 0 || p >= a.pool_pages) {
+    set_status(a.status, EXK_S_PAGE_INDEX);
+    return -1;
+  }
+  return p;
+}
+
 __device__ __forceinline__ int item_split_len(const AttnArgs& a, int T) {
   if (a.T_dev == nullptr) return a.split_len;
   return max(1, ((T + kP - 1) / kP + a.ns - 1) / a.ns) * kP;
@@ -852,12 +871,15 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
       constexpr int nmaps = COMP ? 6 : 2;
       for (int i = 0; i < nmaps; ++i) prefetch_tmap(&tm.m[i]);
     }
-    auto tile_meta = [&](const Item& it_, int s_) {
+    // phys: lane 0's cache page of the stage's first page (its TMA row / 16)
+    auto tile_meta = [&](const Item& it_, int s_, int& phys) {
       int4 r = make_int4(0, 0, 0, 0);
+      const int page = it_.page0 + s_ * WPH + lane % WPH;
+      const int cp = (lane < NWC && page < it_.page0 + it_.npages) ? page_of(a, it_.b, page) : -1;
+      phys = a.pages == nullptr ? it_.b * a.NP + it_.page0 + s_ * WPH : __shfl_sync(0xFFFFFFFFu, cp, 0);
       if constexpr (COMP) {
-        const int page = it_.page0 + s_ * WPH + lane % WPH;
-        if (lane < NWC && page < it_.page0 + it_.npages) {
-          const int64_t idx = (static_cast<int64_t>(it_.b) * a.NP + page) * a.Hkv + it_.hg * HG + lane / WPH;
+        if (cp >= 0) {
+          const int64_t idx = static_cast<int64_t>(cp) * a.Hkv + it_.hg * HG + lane / WPH;
           r = make_int4(__ldg(a.rowmask[0] + idx), __ldg(a.rowoff[0] + idx), __ldg(a.rowmask[1] + idx),
                         __ldg(a.rowoff[1] + idx));
         }
@@ -872,7 +894,8 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
       nst = (it.npages + WPH - 1) / WPH;
       if (nst > 0) break;
     }
-    int4 md = item < a.n_items ? tile_meta(it, 0) : make_int4(0, 0, 0, 0);
+    int mphys = 0;
+    int4 md = item < a.n_items ? tile_meta(it, 0, mphys) : make_int4(0, 0, 0, 0);
     uint32_t gs = 0;  // stages issued
     while (item < a.n_items) {
       const int slot = gs % S;
@@ -888,14 +911,13 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
         }
       }
       if (__any_sync(0xFFFFFFFFu, *abort_flag != 0)) break;
-      const int pg = it.page0 + s * WPH;
-      const int row = it.b * a.TS + pg * kP;
+      const int row = mphys * kP;  // -1 (outside the pool): a box of zeros
       const int h0 = it.hg * HG;
       uint8_t* st = ring + slot * C::kStageBytes;
       if constexpr (COMP) {
         if (lane == 0) {
           mbar_expect_tx(&full[slot], C::kTxBytes);
-          const int prow = it.b * a.NP + pg;
+          const int prow = mphys;
           tma_load_3d(st, &tm.m[0], 0, row, h0, &full[slot]);
           tma_load_3d(st + NWC * 2048, &tm.m[3], 0, row, h0, &full[slot]);
           tma_load_3d(st + NWC * 4096, &tm.m[1], 0, row, h0, &full[slot]);
@@ -948,7 +970,7 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
           if (nst > 0) break;
         }
       }
-      if (item < a.n_items) md = tile_meta(it, s);  // the next stage's metadata, in flight during the wait
+      if (item < a.n_items) md = tile_meta(it, s, mphys);  // the next stage's, in flight during the wait
     }
     // Every copy this warp issued lands before the CTA may exit.
     if (lane == 0) {
@@ -1312,6 +1334,9 @@ int common_args(AttnArgs& a, const uint16_t* q, int B, int TS, int Hkv, int Hq, 
   if (items > (int64_t{1} << 30)) return EXK_EARG;
   a.n_items = static_cast<int>(items);
   a.qk_scale = qk_scale;
+  a.pages = nullptr;
+  a.pages_stride = 0;
+  a.pool_pages = 0;
   for (int i = 0; i < 2; ++i) {
     a.rowmask[i] = nullptr;
     a.rowoff[i] = nullptr;
@@ -1382,9 +1407,25 @@ extern "C" int exk_plan_splits(int B, int Hkv, int T, int num_ctas, int32_t* ns_
 
 namespace {
 
+// A paged call (pages != nullptr) reads its pages from a pool of pool_pages
+// pages through the block table; it needs one page per head per stage (the
+// head group equal to the consumer warps), since consecutive pages of a
+// sequence need not be adjacent in the pool.
+int paged_args(AttnArgs& a, const int32_t* pages, int pages_stride, int pool_pages, int hg, int nwc) {
+  if (pages == nullptr) return 0;
+  if (pool_pages <= 0 || pages_stride < a.NP || hg != nwc) return EXK_EARG;
+  if (static_cast<int64_t>(pool_pages) * kP * a.Hkv > (int64_t{1} << 31) - 1) return EXK_EARG;
+  if ((reinterpret_cast<uintptr_t>(pages) & 3u) != 0) return EXK_EALIGN;
+  a.pages = pages;
+  a.pages_stride = pages_stride;
+  a.pool_pages = pool_pages;
+  return 0;
+}
+
 int split_compressed(const uint16_t* q, const exk_cview* k, const exk_cview* v, int B, int TS, int Hkv, int Hq, int T,
                      int s0, int s1, const exk_partials* ws, int consumer_warps, float qk_scale, int32_t* status,
-                     int device, void* stream, const int32_t* T_dev = nullptr, int T_add = 0, int T_stride = 0) {
+                     int device, void* stream, const int32_t* T_dev = nullptr, int T_add = 0, int T_stride = 0,
+                     const int32_t* pages = nullptr, int pages_stride = 0, int pool_pages = 0) {
   if (k == nullptr || v == nullptr) return EXK_EARG;
   AttnArgs a;
   int r = common_args(a, q, B, TS, Hkv, Hq, T, s0, s1, ws, consumer_warps, qk_scale, status);
@@ -1392,13 +1433,15 @@ int split_compressed(const uint16_t* q, const exk_cview* k, const exk_cview* v, 
   a.T_dev = T_dev;
   a.T_add = T_add;
   a.T_stride = T_stride;
+  const int hg = item_heads(ws, Hkv, consumer_warps);
+  if ((r = paged_args(a, pages, pages_stride, pool_pages, hg, consumer_warps)) != 0) return r;
   int sms = 0;
   if ((r = use_device(device, &sms)) != 0) return r;
-  const int hg = item_heads(ws, Hkv, consumer_warps);
   const int wph = consumer_warps / hg;
   const exk_cview* cv[2] = {k, v};
   AttnMaps maps;
-  const int64_t rows = static_cast<int64_t>(B) * TS, prows = static_cast<int64_t>(B) * (TS / kP);
+  const int64_t rows = pages ? static_cast<int64_t>(pool_pages) * kP : static_cast<int64_t>(B) * TS;
+  const int64_t prows = rows / kP;
   for (int i = 0; i < 2; ++i) {
     const exk_cview* c = cv[i];
     if (!aligned16(c->sm) || !aligned16(c->code) || !aligned16(c->base) || !aligned16(c->raw)) return EXK_EALIGN;
@@ -1423,7 +1466,8 @@ int split_compressed(const uint16_t* q, const exk_cview* k, const exk_cview* v, 
 
 int split_bf16(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int TS, int Hkv, int Hq, int T, int s0,
                int s1, const exk_partials* ws, int consumer_warps, float qk_scale, int32_t* status, int device,
-               void* stream, const int32_t* T_dev = nullptr, int T_add = 0, int T_stride = 0) {
+               void* stream, const int32_t* T_dev = nullptr, int T_add = 0, int T_stride = 0,
+               const int32_t* pages = nullptr, int pages_stride = 0, int pool_pages = 0) {
   if (k == nullptr || v == nullptr) return EXK_EARG;
   AttnArgs a;
   int r = common_args(a, q, B, TS, Hkv, Hq, T, s0, s1, ws, consumer_warps, qk_scale, status);
@@ -1431,13 +1475,14 @@ int split_bf16(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, i
   a.T_dev = T_dev;
   a.T_add = T_add;
   a.T_stride = T_stride;
+  const int hg = item_heads(ws, Hkv, consumer_warps);
+  if ((r = paged_args(a, pages, pages_stride, pool_pages, hg, consumer_warps)) != 0) return r;
   int sms = 0;
   if ((r = use_device(device, &sms)) != 0) return r;
   if (!aligned16(k) || !aligned16(v)) return EXK_EALIGN;
-  const int hg = item_heads(ws, Hkv, consumer_warps);
   const int wph = consumer_warps / hg;
   AttnMaps maps;
-  const int64_t rows = static_cast<int64_t>(B) * TS;
+  const int64_t rows = pages ? static_cast<int64_t>(pool_pages) * kP : static_cast<int64_t>(B) * TS;
   if ((r = head_major_map(&maps.m[0], CU_TENSOR_MAP_DATA_TYPE_UINT16, k, 128, 2, rows, Hkv, 64, kP * wph, hg,
                           CU_TENSOR_MAP_SWIZZLE_128B)) != 0)
     return r;
@@ -1520,6 +1565,34 @@ extern "C" int exk_attention_compressed_devlen(const uint16_t* q, const exk_cvie
                        stream, T_dev, T_add, T_stride);
   return r != 0 ? r : launch_merge(ws, B * Hq, out, static_cast<cudaStream_t>(stream), advance ? T_dev : nullptr,
                                    advance);
+}
+
+extern "C" int exk_attention_compressed_paged(const uint16_t* q, const exk_cview* k, const exk_cview* v,
+                                              int pool_pages, int Hkv, int B, int Hq, const int32_t* block_table,
+                                              int max_pages, const int32_t* seq_lens, const exk_partials* ws,
+                                              uint16_t* out, int consumer_warps, float qk_scale, int32_t* status,
+                                              int device, void* stream) {
+  if (block_table == nullptr || max_pages <= 0 || max_pages > (1 << 26)) return EXK_EARG;
+  const int T_cap = max_pages * kP;
+  int r = devlen_args(ws, out, seq_lens, T_cap, 1, 0);
+  if (r != 0) return r;
+  r = split_compressed(q, k, v, B, T_cap, Hkv, Hq, T_cap, 0, ws->ns, ws, consumer_warps, qk_scale, status, device,
+                       stream, seq_lens, 0, 1, block_table, max_pages, pool_pages);
+  return r != 0 ? r : launch_merge(ws, B * Hq, out, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int exk_attention_bf16_paged(const uint16_t* q, const uint16_t* k, const uint16_t* v, int pool_pages,
+                                        int Hkv, int B, int Hq, const int32_t* block_table, int max_pages,
+                                        const int32_t* seq_lens, const exk_partials* ws, uint16_t* out,
+                                        int consumer_warps, float qk_scale, int32_t* status, int device,
+                                        void* stream) {
+  if (block_table == nullptr || max_pages <= 0 || max_pages > (1 << 26)) return EXK_EARG;
+  const int T_cap = max_pages * kP;
+  int r = devlen_args(ws, out, seq_lens, T_cap, 1, 0);
+  if (r != 0) return r;
+  r = split_bf16(q, k, v, B, T_cap, Hkv, Hq, T_cap, 0, ws->ns, ws, consumer_warps, qk_scale, status, device, stream,
+                 seq_lens, 0, 1, block_table, max_pages, pool_pages);
+  return r != 0 ? r : launch_merge(ws, B * Hq, out, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int exk_attention_bf16_devlen(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int TS,

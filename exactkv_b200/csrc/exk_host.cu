@@ -102,6 +102,7 @@ extern "C" const char* exk_status_string(int code) {
     case EXK_S_CHAIN_TIMEOUT: return "encoder CTA waited more than 2 s for its predecessor's offset";
     case EXK_S_DRAIN_TIMEOUT: return "in-flight TMA copies did not land within 2 s";
     case EXK_S_PEER_TIMEOUT: return "peer merge waited more than 2 s for another GPU's signal";
+    case EXK_S_PAGE_INDEX: return "a block-table entry names a page outside the pool (read as zeros)";
     default: return "unknown device status";
   }
 }

@@ -320,6 +320,77 @@ def attention_compressed_devlen(q, kc, vc, T_dev, T_add=1, out=None, num_warps=N
     return out
 
 
+# ----------------------------------------------------------------------------- paged caches
+
+def _paged_warps(Hkv):
+    """Consumer warps for a paged call: the head group (one page per head per stage)."""
+    if Hkv % 8 == 0:
+        return 8
+    if Hkv % 4 == 0:
+        return 4
+    raise ValueError("paged attention needs a KV head count that is a multiple of 4")
+
+
+def _paged_check(q, block_table, seq_lens):
+    B = q.shape[0]
+    for t, name in ((block_table, "block_table"), (seq_lens, "seq_lens")):
+        if t.dtype != torch.int32 or not t.is_cuda or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous CUDA int32 tensor")
+    if block_table.dim() != 2 or block_table.shape[0] != B or seq_lens.shape != (B,):
+        raise ValueError("block_table must be [B, max_pages] and seq_lens [B]")
+    return block_table.shape[1]
+
+
+def attention_paged(q, kc, vc, block_table, seq_lens, out=None):
+    """Decode attention over paged caches: kc, vc are CompressedKV objects (or
+    their .buffers() dicts) used as page pools — their [B', TS'] buffers seen as
+    B' * TS' / 16 pages — block_table int32 [B, max_pages] names each
+    sequence's pages in the pool, seq_lens int32 [B] its tokens (both on the
+    device). Same results as attention_compressed_devlen over the same pages
+    laid out contiguously (exk_attention_compressed_paged)."""
+    ka, TS, Hkv = _cache_args(kc)
+    va, _, _ = _cache_args(vc)
+    Bp = kc["shape"][0] if isinstance(kc, dict) else kc.B
+    max_pages = _paged_check(q, block_table, seq_lens)
+    _check_q(q, max_pages * P, max_pages * P)
+    B, Hq, _ = q.shape
+    dev = q.device.index
+    stream = torch.cuda.current_stream(q.device).cuda_stream
+    ns, sl = plan_splits(B, Hkv, max_pages * P, dev)
+    ws = _workspace(q.device, stream, B * Hq, ns, sl)
+    out = torch.empty_like(q) if out is None else _check_out(out, q)
+    rc = lib.exk_attention_compressed_paged(q.data_ptr(), ctypes.byref(ka), ctypes.byref(va), Bp * TS // P, Hkv, B,
+                                            Hq, block_table.data_ptr(), max_pages, seq_lens.data_ptr(),
+                                            ctypes.byref(ws[3]), out.data_ptr(), _paged_warps(Hkv),
+                                            D ** -0.5 * LOG2E, status_tensor(dev).data_ptr(), dev, stream)
+    check(rc, "exk_attention_compressed_paged")
+    return out
+
+
+def attention_reference_paged(q, k, v, block_table, seq_lens, out=None):
+    """The bf16 sibling of attention_paged over bf16 pools k, v of shape
+    [B', TS', Hkv, 128] (contiguous; pages of 16 rows), bit-identical for the
+    same values."""
+    if k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16 or not (k.is_contiguous() and v.is_contiguous()):
+        raise ValueError("k and v must be contiguous bf16 [B', TS', Hkv, 128]")
+    Hkv = k.shape[-2]
+    pool_pages = k.numel() // (Hkv * D * P)
+    max_pages = _paged_check(q, block_table, seq_lens)
+    _check_q(q, max_pages * P, max_pages * P)
+    B, Hq, _ = q.shape
+    dev = q.device.index
+    stream = torch.cuda.current_stream(q.device).cuda_stream
+    ns, sl = plan_splits(B, Hkv, max_pages * P, dev)
+    ws = _workspace(q.device, stream, B * Hq, ns, sl)
+    out = torch.empty_like(q) if out is None else _check_out(out, q)
+    rc = lib.exk_attention_bf16_paged(q.data_ptr(), k.data_ptr(), v.data_ptr(), pool_pages, Hkv, B, Hq,
+                                      block_table.data_ptr(), max_pages, seq_lens.data_ptr(), ctypes.byref(ws[3]),
+                                      out.data_ptr(), _paged_warps(Hkv), D ** -0.5 * LOG2E,
+                                      status_tensor(dev).data_ptr(), dev, stream)
+    check(rc, "exk_attention_bf16_paged")
+    return out
+
+
 def attention_reference_devlen(q, k, v, T_dev, T_add=0, out=None, num_warps=None):
     """The bf16 sibling of attention_compressed_devlen on k, v [B, TS, Hkv, 128]
     (bit-identical for the same values, lengths and num_warps)."""

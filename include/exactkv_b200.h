@@ -59,6 +59,7 @@ extern "C" {
 #define EXK_S_CHAIN_TIMEOUT  4  /* (unused: the encoder no longer waits) */
 #define EXK_S_DRAIN_TIMEOUT  5  /* in-flight TMA copies did not land within 2 s */
 #define EXK_S_PEER_TIMEOUT   6  /* a peer merge waited > 2 s for another GPU's signal */
+#define EXK_S_PAGE_INDEX     7  /* a block-table entry named a page outside the pool */
 
 /* One compressed cache (keys or values of one layer): the six buffers of the
  * format above. raw_rows is the number of rows `raw` holds; indices at or
@@ -246,6 +247,31 @@ int exk_selftest_wait_timeout(int32_t *status, uint64_t limit_ns, int device, vo
 
 /* *T_dev += n on `stream` (the end of a device-length decode step). */
 int exk_advance_length(int32_t *T_dev, int n, int device, void *stream);
+
+/* Decode attention over paged caches: the cache buffers `k`, `v` are a pool of
+ * pool_pages 16-token pages (sm [pool_pages * 16, Hkv, 128], code, base
+ * [pool_pages, Hkv, 128], rowmask/rowoff [pool_pages, Hkv], raw as usual — any
+ * [B', TS'] cache seen as B' * TS' / 16 pages), and page p of sequence b is
+ * pool page block_table[b * max_pages + p] (int32 [B, max_pages], device).
+ * seq_lens (int32 [B], device) holds each sequence's tokens (at most
+ * max_pages * 16). `ws` holds the plan for max_pages * 16 tokens, used as in
+ * exk_attention_compressed_devlen with one length per sequence; same results
+ * as that call over the same pages laid out contiguously. The head group must
+ * equal consumer_warps (Hkv a multiple of 8 with 8 warps, of 4 with 4), one
+ * page per head per stage. An entry outside the pool reads as zeros and sets
+ * EXK_S_PAGE_INDEX. No counterpart in the reference (its cache is one
+ * contiguous [B, TS] block per layer). */
+int exk_attention_compressed_paged(const uint16_t *q, const exk_cview *k, const exk_cview *v, int pool_pages,
+                                   int Hkv, int B, int Hq, const int32_t *block_table, int max_pages,
+                                   const int32_t *seq_lens, const exk_partials *ws, uint16_t *out,
+                                   int consumer_warps, float qk_scale, int32_t *status, int device, void *stream);
+
+/* The bf16 sibling of exk_attention_compressed_paged over bf16 pools
+ * k, v [pool_pages * 16, Hkv, 128]; bit-identical for the same values. */
+int exk_attention_bf16_paged(const uint16_t *q, const uint16_t *k, const uint16_t *v, int pool_pages, int Hkv,
+                             int B, int Hq, const int32_t *block_table, int max_pages, const int32_t *seq_lens,
+                             const exk_partials *ws, uint16_t *out, int consumer_warps, float qk_scale,
+                             int32_t *status, int device, void *stream);
 
 /* Compressed cache -> bf16 out [B, T, H, 128] through the attention kernel's
  * decoder. Replaces _dec_only_kernel/decode_to_bf16 (exactkv/kernels.py:197-211, 331-337). */
