@@ -38,6 +38,10 @@ other_configs: BASELINE configs[1] (Qwen 1 x 32768) and Llama 8 x 8192 (the seco
 shape of configs[2]): per-call µs, compressed TB/s and the bf16 sibling's µs,
 with the L2 evicted before each call.
 
+other_configs.paged: the headline batch read through a block table that places
+every page at a random page of the cache (exactkv_b200.kernels.attention_paged)
+against the contiguous device-length call.
+
 FlashInfer (installed library, comparison only): its TRT-LLM-gen bf16 paged
 decode on the same bf16 K/V (16-token pages), timed like our calls. kv_split: configs[3] (1 x 131072 split by KV
 sequence over the ranks).
@@ -360,6 +364,7 @@ def run_ours(a, rank, world, local):
     configs = None
     if not (a.no_configs or a.quick):
         configs = run_configs(a, dev, world)
+        configs["paged"] = time_paged(q, kc, vc, B, T, dev, a.steps)
 
     kv_split = None
     if not (a.no_kv_split or a.quick):
@@ -415,6 +420,44 @@ def run_ours(a, rank, world, local):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def time_paged(q, kc, vc, B, T, dev, reps):
+    """The headline batch read through a block table that scatters every
+    sequence's pages over the whole cache (a random permutation of its pages),
+    against the same device-length call on the contiguous layout: what paging
+    costs the attention."""
+    import torch
+
+    from exactkv_b200 import kernels
+    npg = T // 16
+    pool_pages = kc.B * kc.TS // 16
+    g = torch.Generator().manual_seed(5)
+    perm = torch.randperm(pool_pages, generator=g)[: B * npg].to(torch.int32)
+    table = perm.view(B, npg).to(dev)
+    lens = torch.full((B,), T, dtype=torch.int32, device=dev)
+    out = torch.empty_like(q)
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return round(e0.elapsed_time(e1) / reps * 1e3, 2)
+
+    paged = timed(lambda: kernels.attention_paged(q, kc, vc, table, lens, out=out))
+    # the contiguous device-length call with the same plan (T_cap = T)
+    contiguous = timed(lambda: kernels.attention_compressed_devlen(q, kc, vc, lens, 0, out=out))
+    kernels.check_status(dev)
+    return {"paged_us_per_call": paged, "contiguous_devlen_us_per_call": contiguous,
+            "what": f"{B} x {T} through a block table over a {pool_pages}-page pool (pages randomly placed) "
+                    "vs the contiguous device-length call; back-to-back calls, cache > L2"}
 
 
 def time_encoder(kbf, B, T, Hkv, dev, reps=5):
