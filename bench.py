@@ -666,7 +666,13 @@ def run_kv_split(a, dev, rank, world, T=131072, Hq=32, Hkv=8, reps=20):
     kc, vc = caches
 
     out = torch.empty_like(q)
-    ex = parallel.PeerExchange(plan, Hq) if world > 1 else None
+    ex, peer_err = None, None
+    if world > 1:
+        try:
+            ex = parallel.PeerExchange(plan, Hq)
+        except Exception as e:  # noqa: BLE001 - symmetric memory unavailable: NCCL numbers only
+            peer_err = f"{type(e).__name__}: {str(e)[:160]}"
+    peer = world == 1 or ex is not None
 
     def call_peer():
         if ex is not None:
@@ -696,12 +702,12 @@ def run_kv_split(a, dev, rank, world, T=131072, Hq=32, Hkv=8, reps=20):
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    us = timed(call_peer)
+    us = timed(call_peer) if peer else None
     us_nccl = timed(call_nccl) if world > 1 else None
 
     # the peer path again with an event between the split kernel and the merge
     # (which includes the wait for the peers): this rank's average per phase
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(reps)]
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(reps if peer else 0)]
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
@@ -718,14 +724,15 @@ def run_kv_split(a, dev, rank, world, T=131072, Hq=32, Hkv=8, reps=20):
         e[2].record(stream)
     torch.cuda.synchronize(dev)
     phases = {name: round(sum(e[i].elapsed_time(e[i + 1]) for e in ev) / reps * 1e3, 2)
-              for i, name in enumerate(("split", "merge"))}
+              for i, name in enumerate(("split", "merge"))} if peer else None
     if ex is not None:
         dist.barrier()
         ex.close()
     kernels.check_status(dev)
     nbytes = sum(c.nbytes() for c in caches)        # this rank's compressed cache (an upper bound of what it reads)
-    return {"us_per_call": round(us, 2), "nccl_all_gather_us_per_call": None if us_nccl is None else round(us_nccl, 2),
-            "phases_us_rank0": phases, "context": T, "ranks": world, "splits": plan.ns,
+    return {"us_per_call": round(us if us is not None else us_nccl, 2),
+            "nccl_all_gather_us_per_call": None if us_nccl is None else round(us_nccl, 2),
+            "peer_merge_unavailable": peer_err, "phases_us_rank0": phases, "context": T, "ranks": world, "splits": plan.ns,
             "split_len": plan.split_len, "tokens_per_rank": n, "compressed_mb_per_rank": round(nbytes / 1e6, 1),
             "what": "1 x 131072 decode attention (32 q / 8 kv, 2% raw rows) split by KV sequence over the ranks: "
                     "split kernel, the rank's splits merged to one group partial per row in its symmetric-memory "
