@@ -183,23 +183,22 @@ __global__ void __launch_bounds__(kEncWarps * 32, 4) encode_kernel(const __grid_
     emin2[j] = min_u16x2(emin2[j], __shfl_xor_sync(0xFFFFFFFFu, emin2[j], 16));
   }
 
-  // per channel: base b = max(emax - 15, 0); zero group zm = (a zero exponent
-  // and b > 0); then, as 16-bit lane pairs, -b and -(b + zm) for pass 2
-  uint32_t bw[2] = {0u, 0u}, nb2[4] = {0u, 0u, 0u, 0u}, nbz2[4] = {0u, 0u, 0u, 0u};
-  bool escall = false;
+  // per channel, two channels per word in 16-bit lanes: base b = max(emax - 15,
+  // 0); zero group zm = (a zero exponent and b > 0); the base byte min(b + 128
+  // zm, 255); and for pass 2, -b and -(b + zm)
+  uint32_t byte2[4], nb2[4], nbz2[4], escany = 0u;
 #pragma unroll
-  for (int c = 0; c < 8; ++c) {
-    const int sh = 16 * (c & 1);
-    const int emax = static_cast<int>((emax2[c >> 1] >> (sh + 7)) & 0xFFu);
-    const bool has0 = ((emin2[c >> 1] >> sh) & 0xFFFFu) == 0u;
-    const int bse = max(emax - 15, 0);
-    const bool zm = has0 && bse > 0;  // a zero the plain 15-step window cannot hold
-    const int byte = min(zm ? bse + 128 : bse, 255);
-    bw[c >> 2] |= uint32_t(byte) << (8 * (c & 3));
-    nb2[c >> 1] |= (static_cast<uint32_t>(-bse) & 0xFFFFu) << sh;
-    nbz2[c >> 1] |= (static_cast<uint32_t>(-(bse + (zm ? 1 : 0))) & 0xFFFFu) << sh;
-    escall |= bse >= 128;
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t e2 = emax2[j] >> 7;                                   // lanes: emax
+    const uint32_t b2 = max_s16x2(add_u16x2(e2, 0xFFF1FFF1u), 0u);      // max(emax - 15, 0)
+    const uint32_t zm2 = (min_u16x2(emin2[j], 0x00010001u) ^ 0x00010001u) & min_u16x2(b2, 0x00010001u);
+    byte2[j] = min_u16x2(add_u16x2(b2, zm2 << 7), 0x00FF00FFu);
+    nb2[j] = add_u16x2(~b2, 0x00010001u);
+    nbz2[j] = add_u16x2(~add_u16x2(b2, zm2), 0x00010001u);
+    escany |= b2 & 0xFF80FF80u;                                         // b >= 128: every row escapes
   }
+  const uint32_t bw[2] = {prmt(byte2[0], byte2[1], 0x6420u), prmt(byte2[2], byte2[3], 0x6420u)};
+  const bool escall = escany != 0u;
 
   // pass 2: codes, sign|mantissa bytes and escapes, row by row. Per value:
   // code = max(e - b, 0) (a zero of a zero group gets 0); it escapes when
