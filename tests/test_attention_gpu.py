@@ -19,7 +19,8 @@ from synth_np import CONFIG1, config1_inputs
 
 pytestmark = pytest.mark.gpu
 
-REF_SHAPES = [(1, 4096, 28, 4), (3, 1000, 32, 8), (2, 333, 32, 32), (4, 17, 16, 2)]
+REF_SHAPES = [(1, 4096, 28, 4), (3, 1000, 32, 8), (2, 333, 32, 32), (4, 17, 16, 2),
+              (2, 1, 32, 8), (1, 16, 28, 4)]   # a single token; exactly one full page
 
 
 def _compress(x):

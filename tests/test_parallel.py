@@ -182,7 +182,8 @@ def _check_f64(out, q, k, v, T):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("world,B,T,Hq,Hkv", [(2, 1, 8192, 32, 8), (4, 2, 3000, 28, 4), (8, 1, 131072, 32, 8)])
+@pytest.mark.parametrize("world,B,T,Hq,Hkv", [(2, 1, 8192, 32, 8), (4, 2, 3000, 28, 4), (8, 1, 131072, 32, 8),
+                                              (8, 1, 50, 32, 8)])   # most ranks hold no tokens
 def test_kv_split_emulated_ranks_bit_identical(world, B, T, Hq, Hkv):
     from exactkv_b200 import kernels, synthetic
     k = synthetic.make_kv(B, T, Hkv, seed=21, device="cuda")
@@ -206,7 +207,8 @@ def test_kv_split_emulated_ranks_bit_identical(world, B, T, Hq, Hkv):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("world,B,T,Hq,Hkv", [(2, 1, 8192, 32, 8), (3, 2, 3000, 28, 4), (8, 1, 131072, 32, 8)])
+@pytest.mark.parametrize("world,B,T,Hq,Hkv", [(2, 1, 8192, 32, 8), (3, 2, 3000, 28, 4), (8, 1, 131072, 32, 8),
+                                              (8, 1, 50, 32, 8)])
 def test_peer_merge_emulated_ranks_bit_identical(world, B, T, Hq, Hkv):
     from exactkv_b200 import kernels, synthetic
     k = synthetic.make_kv(B, T, Hkv, seed=41, device="cuda")
