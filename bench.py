@@ -42,9 +42,14 @@ other_configs.paged: the headline batch read through a block table that places
 every page at a random page of the cache (exactkv_b200.kernels.attention_paged)
 against the contiguous device-length call.
 
+reference_triton_compressed_us_per_call: the reference's own Triton
+compressed decode attention on this GPU (same K/V, its own encoder), when the
+unmodified reference package is installed in baseline/_ref; a comparison only.
+
 FlashInfer (installed library, comparison only): its TRT-LLM-gen bf16 paged
-decode on the same bf16 K/V (16-token pages), timed like our calls. kv_split: configs[3] (1 x 131072 split by KV
-sequence over the ranks).
+decode on the same bf16 K/V (16-token pages), timed like our calls.
+
+kv_split: configs[3] (1 x 131072 split by KV sequence over the ranks).
 
 engine: BASELINE configs[4] decode throughput through exactkv_b200.Engine on a
 random-init Llama-3.1-8B (32 layers, hidden 4096, 32 q / 8 kv heads, FFN 14336,
@@ -243,6 +248,34 @@ def flashinfer_decode(q, k, v, T):
         return None, f"{type(e).__name__}: {str(e)[:160]}"
 
 
+def reference_triton_decode(q, k, v, B, T, Hkv):
+    """The reference's own compressed decode attention (its Triton kernels, JIT
+    for this GPU) on caches built by its own encoder from the same K/V, when the
+    unmodified reference package is installed in baseline/_ref (git-ignored).
+    A speed comparison on the same box only. Returns a zero-argument call, or
+    None with the reason."""
+    import torch
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_dir, "exactkv")):
+        return None, "reference package not installed in baseline/_ref"
+    try:
+        if ref_dir not in sys.path:
+            sys.path.insert(0, ref_dir)
+        import exactkv as ref
+        rk, rv = ref.CompressedKV(B, T, Hkv, 128, device=q.device), ref.CompressedKV(B, T, Hkv, 128, device=q.device)
+        for b in range(B):
+            rk.prefill_slot(b, k[b:b + 1, :T])
+            rv.prefill_slot(b, v[b:b + 1, :T])
+
+        def call():
+            return ref.attention_compressed(q, rk, rv, T)
+        call()
+        torch.cuda.synchronize(q.device)
+        return call, None
+    except Exception as e:  # noqa: BLE001 - reported as unavailable
+        return None, f"{type(e).__name__}: {str(e)[:160]}"
+
+
 def run_ours(a, rank, world, local):
     import torch
     import torch.distributed as dist
@@ -353,6 +386,15 @@ def run_ours(a, rank, world, local):
         fi_ms, _ = timed(fi_call, a.steps)
         fi_us = round(fi_ms / a.steps * 1e3, 2)
     fi_call = None                       # holds views of the bf16 cache, freed before the engine leg
+    ref_call, ref_why = reference_triton_decode(q, kbf, vbf, B, T, Hkv) if not a.quick else \
+        (None, "skipped (--quick)")
+    ref_us = None
+    if ref_call is not None:
+        for _ in range(3):
+            ref_call()
+        ref_ms, _ = timed(ref_call, a.steps)
+        ref_us = round(ref_ms / a.steps * 1e3, 2)
+    ref_call = None                      # its caches are freed before the engine leg
 
     value = nbytes * a.steps * world / (total_ms * 1e-3) / 1e12
     peak, peak_src = load_peak()
@@ -401,6 +443,8 @@ def run_ours(a, rank, world, local):
         "frac_of_nominal_8tbs": round(value / world / (NOMINAL_HBM_GBS / 1e3), 4),
         "bf16_sibling_us_per_call": round(sib_us, 2),
         "speedup_vs_bf16_sibling": round(sib_us / (ms_per_step * 1e3), 3),
+        "reference_triton_compressed_us_per_call": ref_us if ref_us is not None else ref_why,
+        "speedup_vs_reference_triton": round(ref_us / (ms_per_step * 1e3), 3) if ref_us is not None else None,
         "flashinfer_trtllm_bf16_us_per_call": fi_us if fi_us is not None else fi_why,
         "speedup_vs_flashinfer_bf16": round(fi_us / (ms_per_step * 1e3), 3) if fi_us is not None else None,
         "roofline": {"bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": peak, "unit": "GB/s",
