@@ -504,6 +504,34 @@ def time_paged(q, kc, vc, B, T, dev, reps):
                     "vs the contiguous device-length call; back-to-back calls, cache > L2"}
 
 
+def reference_encode_us(src, st, B, T, Hkv, dev, reps):
+    """The reference's own encode_pages (Triton) over the same source, when the
+    reference package is installed in baseline/_ref (see reference_triton_decode);
+    else the reason it is not timed."""
+    import torch
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_dir, "exactkv")):
+        return "reference package not installed in baseline/_ref"
+    try:
+        if ref_dir not in sys.path:
+            sys.path.insert(0, ref_dir)
+        import exactkv as ref
+        c = ref.CompressedKV(B, T, Hkv, 128, device=dev, reserve=0.05)
+        times = []
+        for i in range(reps + 2):
+            c.cnt.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            ref.encode_pages(src, st, c._buf(), 0, 0, B, T // 16)
+            e1.record()
+            torch.cuda.synchronize(dev)
+            if i >= 2:
+                times.append(e0.elapsed_time(e1) * 1e3)
+        return round(statistics.median(times), 2)
+    except Exception as e:  # noqa: BLE001 - reported as unavailable
+        return f"{type(e).__name__}: {str(e)[:160]}"
+
+
 def time_encoder(kbf, B, T, Hkv, dev, reps=5):
     """The page encoder over the whole batch's keys in one encode_pages call (a
     prefill of B sequences): bf16 bytes read and compressed bytes written per us."""
@@ -528,8 +556,10 @@ def time_encoder(kbf, B, T, Hkv, dev, reps=5):
     us = statistics.median(times)
     rows = B * T * Hkv
     written = rows * 192 + (rows // 16) * 136 + n * 256
+    ref_us = reference_encode_us(src, st, B, T, Hkv, dev, reps)
     return {"us": round(us, 2), "bf16_read_gbs": round(rows * 256 / us / 1e3, 1),
             "compressed_written_gbs": round(written / us / 1e3, 1), "raw_rows": n,
+            "reference_triton_encode_pages_us": ref_us,
             "what": f"encode_pages over {B} x {T} tokens x {Hkv} heads of keys (4 launches: encode, chunk sums, chunk scan, slot placement + raw copy)"}
 
 
@@ -664,6 +694,9 @@ def run_configs(a, dev, world, reps=30):
         fi_call, fi_why = flashinfer_decode(q, k, v, T)
         us_f = per_call(fi_call) if fi_call is not None else None
         fi_call = None
+        rf_call, rf_why = reference_triton_decode(q, k, v, B, T, Hkv)
+        us_rf = per_call(rf_call) if rf_call is not None else None
+        rf_call = None
         kernels.check_status(dev)
         tbs = nbytes / (us_c * 1e-6) / 1e12
         out[name] = {"batch": B, "context": T, "q_heads": Hq, "kv_heads": Hkv, "splits": ns,
@@ -672,6 +705,7 @@ def run_configs(a, dev, world, reps=30):
                      "bf16_equiv_tbs": round(2 * B * T * Hkv * 256 / (us_c * 1e-6) / 1e12, 3),
                      "bf16_sibling_us_per_call": round(us_r, 2), "speedup_vs_bf16_sibling": round(us_r / us_c, 3),
                      "flashinfer_trtllm_bf16_us_per_call": round(us_f, 2) if us_f is not None else fi_why,
+                     "reference_triton_compressed_us_per_call": round(us_rf, 2) if us_rf is not None else rf_why,
                      "speedup_vs_flashinfer_bf16": round(us_f / us_c, 3) if us_f is not None else None,
                      "raw_row_fraction": round(raw_rows / (2 * B * T * Hkv), 5)}
         del k, v, q, kc, vc
