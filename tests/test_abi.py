@@ -112,3 +112,15 @@ def test_entry_points_reject_bad_arguments_before_any_launch():
     for code in (EARG, EALIGN, -3, -4, EHEADS, -6):
         assert lib.exk_error_string(code).startswith(b"exactkv_b200:")
     assert b"peer" in lib.exk_status_string(6)
+
+
+def test_every_status_code_has_a_description():
+    """Each EXK_S_* code the header defines has its own text (the host reads the
+    device status word and raises with it)."""
+    import re
+    from exactkv_b200._lib import lib
+    codes = {int(v) for v in re.findall(r"#define EXK_S_\w+\s+(\d+)", open(HEADER).read())}
+    assert codes == set(range(len(codes)))
+    texts = [lib.exk_status_string(c) for c in sorted(codes)]
+    assert len(set(texts)) == len(texts) and all(t != b"unknown device status" for t in texts)
+    assert lib.exk_status_string(max(codes) + 1) == b"unknown device status"
