@@ -26,7 +26,10 @@ std::mutex g_mu;
 float* g_dev_ptr[kMaxDev] = {};
 
 // The array's name is a host-side stand-in in host code; the kernels need its
-// device address, looked up once per device with that device current.
+// device address, looked up once per device with that device current. The
+// address is cached for the life of the process and not looked up again after
+// a cudaDeviceReset (the library's other entry points do not survive a reset
+// of their caller's context either).
 int scratch_address(int device, float** out) {
   std::lock_guard<std::mutex> lock(g_mu);
   if (g_dev_ptr[device] == nullptr) {
@@ -46,6 +49,14 @@ extern "C" int exk_attention_compressed_noalloc(const uint16_t* q, const exk_cvi
                                                 int TS, int Hkv, int Hq, int T, int consumer_warps, float qk_scale,
                                                 uint16_t* out, int32_t* status, int device, void* stream) {
   if (B <= 0 || Hkv <= 0 || Hq <= 0 || T <= 0 || device < 0 || device >= exk::kMaxDev) return EXK_EARG;
+  // The shape and output checks of the allocating entry points, before the
+  // scratch size is computed: a bad shape reports its own error (not
+  // EXK_ESCRATCH), and nothing is launched when any argument is refused.
+  if (TS <= 0 || TS % EXK_PAGE != 0 || T > TS || Hq % Hkv != 0) return EXK_EARG;
+  if (Hq / Hkv > 16) return EXK_EHEADS;
+  if (out == nullptr || q == nullptr || k == nullptr || v == nullptr) return EXK_EARG;
+  if ((reinterpret_cast<uintptr_t>(out) & 7u) != 0) return EXK_EALIGN;
+  if (exk::device_reachable(out) != 0) return EXK_EARG;
   int sms = 0;
   int r = exk::use_device(device, &sms);  // makes `device` current before the symbol lookup
   if (r != 0) return r;

@@ -286,7 +286,10 @@ int exk_decode_to_bf16(const exk_cview *c, int B, int TS, int H, int T, uint16_t
  * whose enqueue must not call cudaMalloc). Same arguments and result as
  * exk_attn_split_compressed over the full plan followed by exk_attn_merge into
  * out [B*Hq, 128]. Returns EXK_ESCRATCH when B*Hq x splits x 130 fp32 exceed
- * the array. The first call on a device looks up the array's device address
+ * the array (for example 32 sequences x 32 query heads at 4096 tokens: 1024
+ * rows x 9 splits x 520 B = 4.79 MB is refused; 16 sequences fit). Shape
+ * errors (EXK_EARG, EXK_EHEADS) and output errors are reported before the
+ * size check, and nothing is launched when any argument is refused. The first call on a device looks up the array's device address
  * (make it before any stream capture). All calls on a GPU share the array:
  * calls that overlap on the GPU race. No counterpart in the reference. */
 #define EXK_NOALLOC_SCRATCH_BYTES (4u << 20)

@@ -124,3 +124,25 @@ def test_every_status_code_has_a_description():
     texts = [lib.exk_status_string(c) for c in sorted(codes)]
     assert len(set(texts)) == len(texts) and all(t != b"unknown device status" for t in texts)
     assert lib.exk_status_string(max(codes) + 1) == b"unknown device status"
+
+
+def test_noalloc_rejects_bad_arguments_before_any_launch():
+    """The allocation-free entry point runs the shape and output checks of the
+    allocating ones first: an over-wide GQA ratio is EXK_EHEADS (not the scratch
+    limit), a bad output is refused before the split kernel could be queued."""
+    from exactkv_b200._lib import lib, CView
+    EARG, EALIGN, EHEADS = -1, -2, -5
+    dev_addr = 1 << 40
+    cv = CView(dev_addr, dev_addr, dev_addr, dev_addr, dev_addr, dev_addr, 1024)
+
+    def call(B=1, TS=256, Hkv=8, Hq=32, T=200, out=dev_addr, q=dev_addr):
+        return lib.exk_attention_compressed_noalloc(q, ctypes.byref(cv), ctypes.byref(cv), B, TS, Hkv, Hq, T, 8,
+                                                    0.1, out, None, 0, None)
+
+    assert call(B=4096, Hkv=1, Hq=32, TS=4096, T=4096) == EHEADS   # would also overflow the scratch
+    assert call(Hq=30) == EARG
+    assert call(TS=250, T=200) == EARG
+    assert call(T=300) == EARG
+    assert call(out=0) == EARG
+    assert call(out=dev_addr + 2) == EALIGN
+    assert call(q=0) == EARG
