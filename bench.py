@@ -547,7 +547,7 @@ def time_encoder(kbf, B, T, Hkv, dev, reps=5):
         c.cnt.zero_()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        kernels.encode_pages(src, st, c._buf(), 0, 0, B, T // 16)
+        kernels.encode_pages(src, st, c.encoder_buffers(), 0, 0, B, T // 16)
         e1.record()
         torch.cuda.synchronize(dev)
         if i >= 2:

@@ -128,11 +128,37 @@ def _view_from_dict(c):
     return cv, c["shape"][1], c["shape"][2]
 
 
+_ARGS_VIEWS = {}  # id(kernel_args() tuple) -> (the tuple, its exk_cview)
+
+
+def _view_from_args(kargs):
+    """exk_cview of a kernel_args() tuple (sm, code, base, rowmask, rowoff, raw as
+    int16 [rows, 128]), the form a reference CompressedKV hands its kernels
+    (exactkv/cache.py:39-47). A cache rebuilds that tuple only when its raw pool
+    grows, so the view is kept per tuple object."""
+    hit = _ARGS_VIEWS.get(id(kargs))
+    if hit is not None and hit[0] is kargs:
+        return hit[1]
+    sm, code, base, rowmask, rowoff, raw = kargs
+    cv = CView(sm.data_ptr(), code.data_ptr(), base.data_ptr(), rowmask.data_ptr(), rowoff.data_ptr(),
+               raw.data_ptr(), raw.shape[0])
+    if len(_ARGS_VIEWS) > 256:
+        _ARGS_VIEWS.clear()
+    _ARGS_VIEWS[id(kargs)] = (kargs, cv)
+    return cv
+
+
 def _cache_args(c):
-    """(exk_cview, TS, Hkv) from a CompressedKV (cached there) or from its .buffers() dict."""
+    """(exk_cview, TS, Hkv) from a cache object or from its .buffers() dict, as the
+    reference's _cache_args takes them (exactkv/kernels.py:302-307): this package's
+    CompressedKV (its view is kept on the cache), or any cache with the reference's
+    kernel_args() / .TS / .H, the reference's own CompressedKV included."""
     if isinstance(c, dict):
         return _view_from_dict(c)
-    return c.kernel_view(), c.TS, c.H
+    view = getattr(c, "kernel_view", None)
+    if view is not None:
+        return view(), c.TS, c.H
+    return _view_from_args(c.kernel_args()), c.TS, c.H
 
 
 def _check_q(q, T, TS):

@@ -108,7 +108,7 @@ def test_gpu_encoder_strided_and_unaligned_sources():
         B, T, H, D = src.shape
         c = ekv.CompressedKV(B, T, H, D, reserve=1.0)
         st = (src.stride(0), 16 * src.stride(1), src.stride(1), src.stride(2))
-        kernels.encode_pages(src, st, c._buf(), 0, 0, B, T // 16)
+        kernels.encode_pages(src, st, c.encoder_buffers(), 0, 0, B, T // 16)
         n = int(c.cnt.item())
         for f in ("sm", "code", "base", "rowmask", "rowoff"):
             assert np.array_equal(getattr(c, f).cpu().numpy(), ref[f]), f
@@ -125,7 +125,7 @@ def test_gpu_encoder_pool_overflow_counts_and_skips():
     nraw = ref["raw"].shape[0]
     assert nraw > 8
     c = ekv.CompressedKV(1, 64, 4, 128)
-    buf = c._buf()
+    buf = c.encoder_buffers()
     buf["cap"] = 8                                        # a pool smaller than needed
     sentinel = torch.full_like(c.raw, 7.0)
     c.raw.copy_(sentinel)

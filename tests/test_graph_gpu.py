@@ -88,7 +88,7 @@ def test_graphed_steps_match_host_path():
             assert torch.equal(getattr(a, f), getattr(g, f)), f
         # encoded pages share pool slots; the open tail page points into each pool's own tail area
         assert torch.equal(a.rowoff[:, :a.T // 16], g.rowoff[:, :g.T // 16])
-        assert torch.equal(g.rowoff[:, g.T // 16], g._toff)
+        assert torch.equal(g.rowoff[:, g.T // 16], g.tail_offsets())
         n = int(a.cnt.item())
         assert n == int(g.cnt.item())
         assert torch.equal(a.raw[:n], g.raw[:n])

@@ -40,7 +40,7 @@ def _place(x, pool_c, pool_bf, perm):
             i += 1
             table[b, p] = phys
             src = x[b:b + 1, p * 16:]
-            kernels.encode_pages(src, st, pool_c._buf(), phys // npp, phys % npp, 1, 1)
+            kernels.encode_pages(src, st, pool_c.encoder_buffers(), phys // npp, phys % npp, 1, 1)
             pool_bf.view(-1, 16, x.shape[2], 128)[phys] = x[b, p * 16:(p + 1) * 16]
     assert int(pool_c.cnt.item()) <= pool_c.cap
     return table.cuda()
