@@ -59,9 +59,13 @@ context is filled with the synthetic KV through the prefill encoder (the
 decode step's cost does not depend on how the context was produced), then
 greedy steps are timed with CUDA events; tok/s summed over ranks.
 
---impl reference: the reference algorithm on the host CPU (the numpy oracle:
-codec decode + split-K attention) over all host cores, a bounded sample per
-step (one sequence of the batch); rank 0 only.
+--impl reference: the reference's own CPU path on the host cores — its PyTorch
+codec (exactkv.codec.decode_reference, loaded unmodified from baseline/_ref)
+plus its split-K attention restated in torch (the reference has no CPU
+attention; oracle/torch_attention.py), every host core as a torch thread — a
+bounded sample per step (one sequence of the batch); rank 0 only. Without
+baseline/_ref, the numpy oracle port of the same path. cpu_baseline (our arm)
+reports the same reference path with the numpy port beside it.
 """
 import argparse
 import json
@@ -80,7 +84,7 @@ NOMINAL_HBM_GBS = 8000.0
 FALLBACK_HBM_GBS = 6650.0
 WORKLOAD = dict(workload="llama3.1-8b decode attention, compressed KV", batch_per_gpu=32, context=4096, q_heads=32,
                 kv_heads=8, head_dim=128, page=16, rope_theta=5e5, zero_keys=4e-4, forced_raw_rows=3e-3)
-PROFILE_SUMMARY = os.path.join(ROOT, "profiles", "attn_split_compressed__llama_32x4096.md")
+TRAFFIC_RECORD = os.path.join(ROOT, "profiles", "attn_split_compressed__llama_32x4096.traffic.json")
 
 
 def parse_args():
@@ -98,6 +102,9 @@ def parse_args():
     ap.add_argument("--no-configs", action="store_true")
     ap.add_argument("--engine-steps", type=int, default=24)
     ap.add_argument("--num-warps", type=int, default=8)
+    ap.add_argument("--record-traffic", metavar="NCU_REP",
+                    help="write the split kernel's per-launch DRAM bytes from an ncu report and exit")
+    ap.add_argument("--traffic-batch", type=int, default=16, help="batch of the --record-traffic capture")
     ap.add_argument("--quick", action="store_true",
                     help="few launches for profiling: no warm loop, L2-flushed pass, e2e or CPU baseline")
     return ap.parse_args()
@@ -117,16 +124,62 @@ def load_peak():
 
 
 def profiled_traffic():
-    """dram bytes per launch of the split kernel at this workload, from the committed
-    ncu summary (line `traffic_bytes_per_launch: N`), or None."""
+    """(dram bytes per launch of the split kernel at this workload, record) from the
+    data file `python bench.py --record-traffic <capture>.ncu-rep` writes, or
+    (None, None) when no capture of the current source has been recorded."""
     try:
-        with open(PROFILE_SUMMARY) as f:
-            for line in f:
-                if line.strip().startswith("traffic_bytes_per_launch:"):
-                    return int(float(line.split(":", 1)[1].strip().split()[0]))
-    except OSError:
-        pass
-    return None
+        with open(TRAFFIC_RECORD) as f:
+            rec = json.load(f)
+    except (OSError, ValueError):
+        return None, None
+    if rec.get("source_sha256") != kernel_source_digest():
+        return None, "stale: recorded for other kernel source"
+    return int(rec["traffic_bytes_per_launch"]), rec
+
+
+def kernel_source_digest():
+    """SHA-256 of the attention kernel's sources (a recorded capture is used only
+    for the source it measured)."""
+    import hashlib
+    h = hashlib.sha256()
+    for f in ("exk_attention.cu", "exk_device.cuh"):
+        with open(os.path.join(ROOT, "exactkv_b200", "csrc", f), "rb") as fh:
+            h.update(fh.read())
+    return h.hexdigest()
+
+
+def record_traffic(rep, batch, scale):
+    """Reads dram__bytes_read.sum + dram__bytes_write.sum of the split kernel's
+    launches from an ncu report (ncu -i <rep> --page raw --csv) and writes the
+    per-launch mean, scaled by `scale` (the headline batch over the captured
+    batch; traffic grows with the pages read), to TRAFFIC_RECORD."""
+    import csv
+    import io
+    import subprocess
+    out = subprocess.run(["ncu", "-i", rep, "--page", "raw", "--csv"], capture_output=True, text=True,
+                         check=True).stdout
+    rows = list(csv.reader(io.StringIO(out)))
+    hdr, units = rows[0], rows[1]
+    col = {h: i for i, h in enumerate(hdr)}
+    mult = {"byte": 1, "Kbyte": 1e3, "Mbyte": 1e6, "Gbyte": 1e9}
+    per_launch = []
+    for r in rows[2:]:
+        if "attn_split_kernel" not in r[col["Kernel Name"]] or "ILb1" not in r[col["Kernel Name"]] and \
+                "<true" not in r[col["Kernel Name"]]:
+            continue
+        tot = 0.0
+        for m in ("dram__bytes_read.sum", "dram__bytes_write.sum"):
+            tot += float(r[col[m]].replace(",", "")) * mult[units[col[m]]]
+        per_launch.append(tot)
+    if not per_launch:
+        raise SystemExit(f"no compressed split-kernel launch with dram byte counts in {rep}")
+    rec = {"traffic_bytes_per_launch": int(statistics.mean(per_launch) * scale),
+           "captured_bytes_per_launch": int(statistics.mean(per_launch)), "launches": len(per_launch),
+           "captured_batch": batch, "scale": scale, "source_sha256": kernel_source_digest(),
+           "report": os.path.basename(rep)}
+    with open(TRAFFIC_RECORD, "w") as f:
+        json.dump(rec, f, indent=1)
+    print(json.dumps(rec))
 
 
 class ClockSampler:
@@ -399,7 +452,7 @@ def run_ours(a, rank, world, local):
     value = nbytes * a.steps * world / (total_ms * 1e-3) / 1e12
     peak, peak_src = load_peak()
     achieved_gbs = nbytes / (kernel_us * 1e-6) / 1e9      # all algorithmic bytes are this kernel's
-    traffic = profiled_traffic()
+    traffic, traffic_rec = profiled_traffic()
 
     encoder = None if a.quick else time_encoder(kbf, B, T, Hkv, dev)
 
@@ -423,7 +476,7 @@ def run_ours(a, rank, world, local):
 
     cpu = None
     if rank == 0 and world == 1 and not (a.no_cpu_baseline or a.quick):
-        cpu = cpu_sample(T, Hkv, Hq)
+        cpu = cpu_baselines(T, Hkv, Hq)
     rec = {
         "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world, "steps": a.steps,
         "warmup": a.warmup, "ms_per_step": round(ms_per_step, 5), "higher_is_better": True, "scaling": "weak",
@@ -449,7 +502,10 @@ def run_ours(a, rank, world, local):
         "speedup_vs_flashinfer_bf16": round(fi_us / (ms_per_step * 1e3), 3) if fi_us is not None else None,
         "roofline": {"bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved_gbs / peak, 4), "peak_source": f"{peak_src} hbm_gbs (copy, read+write)",
-                     "traffic": traffic, "kernel": "exk::attn_split_kernel<compressed>"},
+                     "traffic": traffic, "kernel": "exk::attn_split_kernel<compressed>",
+                     "traffic_source": traffic_rec if not isinstance(traffic_rec, dict) else
+                     f"ncu capture {traffic_rec['report']} at batch {traffic_rec['captured_batch']}, "
+                     f"x{traffic_rec['scale']} to the headline batch (recorded for this kernel source)"},
         "gpu_launches": 2 * a.steps,
         "encoder": encoder,
         "clocks": clocks.summary(),
@@ -916,29 +972,126 @@ def cpu_sample(T, Hkv, Hq, seconds=10.0, nseq=4):
                       f"with {procs} processes"}
 
 
+def _reference_codec():
+    """The reference's own codec module (exactkv/codec.py, plain PyTorch), loaded by
+    file path from the unmodified install in baseline/_ref; None when absent. Only
+    codec.py is loaded (it imports torch alone), not the package with its Triton
+    kernels."""
+    import importlib.util
+    path = os.path.join(ROOT, "baseline", "_ref", "exactkv", "codec.py")
+    if not os.path.isfile(path):
+        return None
+    spec = importlib.util.spec_from_file_location("exactkv_reference_codec", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def _reference_cpu_setup(T, Hkv, Hq):
+    """One sequence (T tokens x Hkv heads, K and V) encoded by the reference's
+    encode_reference on the CPU; returns (codec, (ck, cv, q), compressed bytes)."""
+    import torch
+
+    from exactkv_b200 import synthetic
+    codec = _reference_codec()
+    if codec is None:
+        return None
+    TS = -(-T // 16) * 16
+    k = synthetic.make_kv(1, TS, Hkv, seed=4242, theta=5e5, key=True, device="cpu")
+    v = synthetic.make_kv(1, TS, Hkv, seed=4243, theta=5e5, key=False, device="cpu")
+    q = synthetic.make_q(1, Hq, seed=4244, device="cpu")
+    ck, cv = codec.encode_reference(k), codec.encode_reference(v)
+    nbytes = 0
+    for c in (ck, cv):
+        raw_rows = int(c["raw"].shape[0])
+        nbytes += TS * Hkv * 192 + c["base"].numel() + 8 * c["rowmask"].numel() + raw_rows * 256
+    torch.set_num_threads(os.cpu_count() or 1)
+    return codec, (ck, cv, q), nbytes
+
+
+def _reference_cpu_step(codec, data, T):
+    """The reference's PyTorch decode_reference of K and V, then the split-K
+    attention restated in torch (oracle/torch_attention.py)."""
+    from oracle import torch_attention
+    ck, cv, q = data
+    return torch_attention.attention(q, codec.decode_reference(ck), codec.decode_reference(cv), T)
+
+
+def cpu_reference_sample(T, Hkv, Hq, seconds=10.0):
+    """The reference's own CPU codec (decode_reference, unmodified) + the torch
+    attention restatement, on one sequence of the batch, repeated for about
+    `seconds` with every host core as a torch thread. None without baseline/_ref."""
+    import torch
+    setup = _reference_cpu_setup(T, Hkv, Hq)
+    if setup is None:
+        return None
+    codec, data, nbytes = setup
+    _reference_cpu_step(codec, data, T)                  # warm
+    secs = []
+    t_end = time.perf_counter() + seconds
+    while time.perf_counter() < t_end or len(secs) < 2:
+        t0 = time.perf_counter()
+        _reference_cpu_step(codec, data, T)
+        secs.append(time.perf_counter() - t0)
+    s = sum(secs)
+    threads = torch.get_num_threads()
+    return {"value": round(nbytes * len(secs) / s / 1e12, 8), "unit": UNIT, "cores": threads, "kind": "reference",
+            "sample": f"{len(secs)} passes over 1 of the 32 sequences ({T} tokens x {Hkv} KV heads, K and V): "
+                      f"the reference's exactkv.codec.decode_reference (PyTorch, unmodified, from baseline/_ref) "
+                      f"+ its split-K attention restated in torch (oracle/torch_attention.py), "
+                      f"{s / len(secs) * 1e3:.1f} ms per sequence with {threads} torch threads"}
+
+
+def cpu_baselines(T, Hkv, Hq):
+    """cpu_baseline: the reference's own CPU codec path when baseline/_ref is
+    installed (kind "reference"), with the numpy port beside it; else the port."""
+    ref = cpu_reference_sample(T, Hkv, Hq)
+    port = cpu_sample(T, Hkv, Hq)
+    if ref is None:
+        return port
+    ref["port"] = port
+    return ref
+
+
 def run_reference(a, rank, world):
     if rank != 0:
         return
     T, Hkv, Hq = a.context, 8, 32
-    cb, d, per_seq, pool, procs = _cpu_setup(T, Hkv, Hq, 1)
-    try:
+    setup = _reference_cpu_setup(T, Hkv, Hq)
+    if setup is not None:
+        import torch
+        codec, data, per_seq = setup
+        kind, procs = "reference", torch.get_num_threads()
         for _ in range(max(1, a.warmup)):
-            cb.run_step(pool, d, [0], Hkv)
+            _reference_cpu_step(codec, data, T)
         t0 = time.perf_counter()
         for _ in range(a.steps):
-            cb.run_step(pool, d, [0], Hkv)
+            _reference_cpu_step(codec, data, T)
         total = time.perf_counter() - t0
-    finally:
-        pool.close()
-        pool.join()
+        sample = (f"each step: 1 sequence of the 32 x 4096 batch (8 KV heads, K and V): the reference's own "
+                  f"exactkv.codec.decode_reference (PyTorch, unmodified, from baseline/_ref) + its split-K "
+                  f"attention restated in torch (oracle/torch_attention.py), {procs} torch threads")
+    else:
+        cb, d, per_seq, pool, procs = _cpu_setup(T, Hkv, Hq, 1)
+        kind = "port"
+        try:
+            for _ in range(max(1, a.warmup)):
+                cb.run_step(pool, d, [0], Hkv)
+            t0 = time.perf_counter()
+            for _ in range(a.steps):
+                cb.run_step(pool, d, [0], Hkv)
+            total = time.perf_counter() - t0
+        finally:
+            pool.close()
+            pool.join()
+        sample = (f"each step: 1 sequence of the 32 x 4096 batch (8 KV heads, K and V), numpy oracle restatement "
+                  f"of the reference codec decode + split-K attention over {procs} processes (baseline/_ref absent)")
     value = per_seq * a.steps / total / 1e12
-    sample = (f"each step: 1 sequence of the 32 x 4096 batch (8 KV heads, K and V), numpy oracle restatement "
-              f"of the reference codec decode + split-K attention over {procs} processes")
     rec = {"metric": METRIC, "value": round(value, 8), "unit": UNIT, "n_gpus": world, "steps": a.steps,
            "warmup": a.warmup, "ms_per_step": round(total / a.steps * 1e3, 3), "higher_is_better": True,
            "scaling": "weak", "vs_baseline": None, "dtype": "u8 codes -> fp32", "data": "synthetic",
            "config": dict(WORKLOAD, global_batch=32, parallelism="host CPU"), "impl": "reference",
-           "cpu_baseline": {"value": round(value, 8), "unit": UNIT, "cores": procs, "kind": "port",
+           "cpu_baseline": {"value": round(value, 8), "unit": UNIT, "cores": procs, "kind": kind,
                             "sample": sample},
            "e2e": {"value": round(value, 8), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(rec), flush=True)
@@ -946,6 +1099,9 @@ def run_reference(a, rank, world):
 
 def main():
     a = parse_args()
+    if a.record_traffic:
+        record_traffic(a.record_traffic, a.traffic_batch, 32 / a.traffic_batch)
+        return 0
     rank, world, local = dist_env()
     if a.impl == "reference":
         run_reference(a, rank, world)

@@ -190,10 +190,14 @@ __device__ __forceinline__ Item decode_item(const AttnArgs& a, int item) {
 //   covers channel quad 16t+4kk (kk<4) or 64+16t+4(kk-4); kw[row][2kk] holds
 //   the quad's channels 0-1, kw[row][2kk+1] channels 2-3 (bf16 pairs).
 // V (A operand of O^T = V^T P^T): token pairs (sigma(2t), sigma(2t+1)) and
-//   the same +8; m-tile mm covers channels chA = 8g+2mm (mm<4) or
-//   64+8g+2(mm-4) and chB = chA+1; vw[pair][mm][0] = (V[tokA][chA], V[tokB][chA]),
+//   the same +8; m-tile mm covers channels chA = v_channel(mm, g) and chB =
+//   chA+1 (bf16 kernel: 8g+2mm (mm<4) or 64+8g+2(mm-4); compressed kernel:
+//   16mm+2g, see load_v_comp); vw[pair][mm][0] = (V[tokA][chA], V[tokB][chA]),
 //   vw[pair][mm][1] the same for chB.
 
+// KKILL = false: the page's K base bytes have no zero group (checked by the
+// caller), so the code-0 rule is skipped.
+template <bool KKILL = true>
 __device__ __forceinline__ void load_k_comp(const Slot& s, int g, int t, uint32_t (&kw)[2][16]) {
   const uint8_t* sm = s.p[0];
   const uint8_t* cd = s.p[1];
@@ -211,9 +215,12 @@ __device__ __forceinline__ void load_k_comp(const Slot& s, int g, int t, uint32_
     const uint32_t smw[8] = {sl.x, sl.y, sl.z, sl.w, sh.x, sh.y, sh.z, sh.w};
     const uint32_t cwv[4] = {cw.x, cw.y, cw.z, cw.w};
 #pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-      const uint32_t c = kk < 4 ? lo_nibbles(cwv[kk & 3]) : hi_nibbles(cwv[kk & 3]);
-      dec4(smw[kk], c, bw[kk] & 0x7F7F7F7Fu, bw[kk], kw[rr][2 * kk], kw[rr][2 * kk + 1]);
+    for (int kk = 0; kk < 4; ++kk) {
+      const uint32_t adj_lo = KKILL ? bw[kk] & 0x7F7F7F7Fu : bw[kk];
+      const uint32_t adj_hi = KKILL ? bw[kk + 4] & 0x7F7F7F7Fu : bw[kk + 4];
+      dec4f<KKILL, false, 0x5140u, 0x7362u>(smw[kk], cwv[kk], adj_lo, bw[kk], kw[rr][2 * kk], kw[rr][2 * kk + 1]);
+      dec4f<KKILL, true, 0x5140u, 0x7362u>(smw[kk + 4], cwv[kk], adj_hi, bw[kk + 4], kw[rr][2 * kk + 8],
+                                           kw[rr][2 * kk + 9]);
     }
   }
 }
@@ -235,10 +242,10 @@ __device__ __forceinline__ void load_k_bf16(const Slot& s, int g, int t, uint32_
   }
 }
 
-// VKILL = false: the page's V base bytes have no zero group (checked by the
-// caller), so the code-0 rule is skipped and the base bytes are used as they are.
+// The V loader without ldmatrix (EXK_V_LDSM = 0): per-lane 8-byte loads and a
+// byte interleave of the two tokens of a pair; channel map 8g + 2mm.
 template <bool VKILL>
-__device__ __forceinline__ void load_v_comp(const Slot& s, int g, int t, uint32_t (&vw)[2][8][2]) {
+__device__ __forceinline__ void load_v_comp_lds(const Slot& s, int g, int t, uint32_t (&vw)[2][8][2]) {
   const uint8_t* sm = s.p[3];
   const uint8_t* cd = s.p[4];
   const uint8_t* bs = s.p[5];
@@ -274,6 +281,80 @@ __device__ __forceinline__ void load_v_comp(const Slot& s, int g, int t, uint32_
     for (int mm = 4; mm < 8; ++mm)
       dec4<VKILL>(ih[mm - 4], hi_nibbles(jc[mm - 4]), VKILL ? eb[mm] & 0x7F7F7F7Fu : eb[mm], eb[mm], vw[pp][mm][0],
                   vw[pp][mm][1]);
+  }
+}
+
+// Compressed V through ldmatrix.trans. The bytes of the sm and code tiles are
+// read as b16 elements (two channels each), so a transposed 8x8 load gives lane
+// (g, t) the word [A(ch), A(ch+1), B(ch), B(ch+1)] of tokens A, B (the matrix
+// rows 2t, 2t+1) and channels ch = 16c + 2g, ch + 1 of 16-byte chunk c — the
+// token pair of a V^T fragment with no byte interleaving, and the base bytes
+// come duplicated per token ([b(ch), b(ch+1), b(ch), b(ch+1)]) from a matrix
+// whose eight row addresses are all the chunk of the base row. m-tile c of
+// O^T = V^T P^T then holds channel 16c + 2g in row g and 16c + 2g + 1 in row
+// g + 8 (v_channel). Matrix row j of token half pp is page token sigma(j) + 8pp,
+// the token order of P^T.
+struct VOffs {
+  uint32_t sm[4];  // sm tile:   load k -> chunks 2k, 2k+1 (x token halves 0, 1)
+  uint32_t cd[2];  // code tile: load k -> chunks 2k, 2k+1 (x token halves)
+  uint32_t bs[2];  // base row:  load k -> chunks 4k .. 4k+3
+};
+
+__device__ __forceinline__ VOffs v_offsets(int lane) {
+  const int mi = lane >> 3, ri = lane & 7;
+  const int row = sigma(ri) + 8 * (mi & 1);
+  VOffs o;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int c = 2 * k + (mi >> 1);
+    o.sm[k] = static_cast<uint32_t>(row * 128 + ((c ^ (row & 7)) << 4));
+  }
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const int c = 2 * k + (mi >> 1);
+    o.cd[k] = static_cast<uint32_t>(row * 64 + ((c ^ ((row >> 1) & 3)) << 4));
+    o.bs[k] = static_cast<uint32_t>(16 * (4 * k + mi));
+  }
+  return o;
+}
+
+// Channel of row g of V m-tile c (row g + 8 holds the next channel).
+#ifndef EXK_V_LDSM
+#define EXK_V_LDSM 1
+#endif
+template <bool COMP>
+__device__ __forceinline__ int v_channel(int c, int g) {
+  if constexpr (COMP && EXK_V_LDSM) return 16 * c + 2 * g;
+  return c < 4 ? 8 * g + 2 * c : 64 + 8 * g + 2 * (c - 4);
+}
+
+// The V base words of a page: eb[c] = [b(16c+2g), b(16c+2g+1)] twice.
+__device__ __forceinline__ void load_v_base(const Slot& s, const VOffs& vo, uint32_t (&eb)[8]) {
+  const uint32_t bs = smem_addr(s.p[5]);
+  ldsm_x4_t(bs + vo.bs[0], eb[0], eb[1], eb[2], eb[3]);
+  ldsm_x4_t(bs + vo.bs[1], eb[4], eb[5], eb[6], eb[7]);
+}
+
+// VKILL = false: the page's V base bytes have no zero group (checked by the
+// caller), so the code-0 rule is skipped and the base bytes are used as they are.
+template <bool VKILL>
+__device__ __forceinline__ void load_v_comp(const Slot& s, const VOffs& vo, const uint32_t (&eb)[8],
+                                            uint32_t (&vw)[2][8][2]) {
+  const uint32_t sm = smem_addr(s.p[3]), cd = smem_addr(s.p[4]);
+  uint32_t smr[2][8], cdr[2][4];  // [token half][chunk]
+#pragma unroll
+  for (int k = 0; k < 4; ++k) ldsm_x4_t(sm + vo.sm[k], smr[0][2 * k], smr[1][2 * k], smr[0][2 * k + 1], smr[1][2 * k + 1]);
+#pragma unroll
+  for (int k = 0; k < 2; ++k) ldsm_x4_t(cd + vo.cd[k], cdr[0][2 * k], cdr[1][2 * k], cdr[0][2 * k + 1], cdr[1][2 * k + 1]);
+#pragma unroll
+  for (int pp = 0; pp < 2; ++pp) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      dec4f<VKILL, false, 0x6240u, 0x7351u>(smr[pp][c], cdr[pp][c], VKILL ? eb[c] & 0x7F7F7F7Fu : eb[c], eb[c],
+                                            vw[pp][c][0], vw[pp][c][1]);
+      dec4f<VKILL, true, 0x6240u, 0x7351u>(smr[pp][c + 4], cdr[pp][c], VKILL ? eb[c + 4] & 0x7F7F7F7Fu : eb[c + 4],
+                                           eb[c + 4], vw[pp][c + 4][0], vw[pp][c + 4][1]);
+    }
   }
 }
 
@@ -377,6 +458,42 @@ __device__ __forceinline__ void fix_v_rows(uint32_t fl, uint32_t rm, const RawRo
   }
 }
 
+// Row r of V (its 256-byte bf16 row at `row`, or zeros when row is null)
+// written into the ldmatrix-layout fragments of the compressed kernel: the
+// lane's word for chunk c is the channel pair (16c + 2g, 16c + 2g + 1); token
+// A of the pair takes the low halves, token B the high halves.
+__device__ __forceinline__ void put_v_row_t(const uint32_t* row, bool b_side, int g, uint32_t (&v)[8][2]) {
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    const uint32_t w = row != nullptr ? row[8 * c + g] : 0u;
+    if (b_side) {
+      v[c][0] = prmt(w, v[c][0], 0x1054u);
+      v[c][1] = prmt(w, v[c][1], 0x3254u);
+    } else {
+      v[c][0] = prmt(w, v[c][0], 0x7610u);
+      v[c][1] = prmt(w, v[c][1], 0x7632u);
+    }
+  }
+}
+
+// The compressed kernel's V fix-up (ldmatrix layout): rows flagged in `fl`
+// are replaced, raw rows (bit set in rm) by their pool row, rows past the
+// valid tokens by zeros.
+__device__ __forceinline__ void fix_v_rows_t(uint32_t fl, uint32_t rm, const RawRows& src, int32_t* status, int vr,
+                                             int g, int t, uint32_t (&vw)[2][8][2]) {
+#pragma unroll
+  for (int pp = 0; pp < 2; ++pp) {
+#pragma unroll
+    for (int ab = 0; ab < 2; ++ab) {
+      const int r = sigma(2 * t + ab) + 8 * pp;
+      if ((fl >> r) & 1u) {
+        const uint4* row = (r < vr && ((rm >> r) & 1u)) ? raw_row(rm, src, r, status) : nullptr;
+        put_v_row_t(reinterpret_cast<const uint32_t*>(row), ab != 0, g, vw[pp]);
+      }
+    }
+  }
+}
+
 // ------------------------------------------------------------------ per-warp state
 
 template <int NT>
@@ -450,6 +567,20 @@ __device__ __forceinline__ void patch_v_staged(uint32_t rm, uint32_t tag, const 
   }
 }
 
+template <int R>
+__device__ __forceinline__ void patch_v_staged_t(uint32_t rm, uint32_t tag, const uint16_t* area, int g, int t,
+                                                 uint32_t (&vw)[2][8][2]) {
+#pragma unroll
+  for (int pp = 0; pp < 2; ++pp) {
+#pragma unroll
+    for (int ab = 0; ab < 2; ++ab) {
+      const int r = sigma(2 * t + ab) + 8 * pp;
+      if ((rm >> r) & 1u)
+        put_v_row_t(reinterpret_cast<const uint32_t*>(staged_row<R>(area, tag, rm, r)), ab != 0, g, vw[pp]);
+    }
+  }
+}
+
 // Page bodies of the warp. kFast: a full page without raw rows (no fixup code
 // at all, so nothing splits the decode / mma schedule). kStaged: a full page
 // whose raw rows were all staged in shared memory by the producer; the lanes
@@ -460,14 +591,29 @@ __device__ __forceinline__ void patch_v_staged(uint32_t rm, uint32_t tag, const 
 // room, zero groups in V).
 enum PageMode { kFast = 0, kStaged = 1, kGeneral = 2 };
 
-template <bool COMP, int NT, int MODE>
+// Rescale the running output only when some row's maximum grew: with
+// alpha = 1 exactly (ex2(0) = 1) the skipped multiplies would leave every bit as
+// it is, so the result is the same either way. EXK_LAZY_RESCALE = 0 restores the
+// unconditional rescale.
+#ifndef EXK_LAZY_RESCALE
+#define EXK_LAZY_RESCALE 1
+#endif
+// 1: pages whose K holds no zero group take a K decoder without the code-0 rule
+// (one more copy of the fast body).
+#ifndef EXK_KZERO_BRANCH
+#define EXK_KZERO_BRANCH 0
+#endif
+
+// KKILL: the page's K holds a zero group (compressed kernel; else ignored).
+template <bool COMP, int NT, int MODE, bool KKILL>
 __device__ __forceinline__ void attend_page(const Slot& s, const PageMeta& pm, int vr, const AttnArgs& a,
-                                            const uint32_t (&qf)[NT][16], WarpState<NT>& st, int g, int t) {
+                                            const uint32_t (&qf)[NT][16], WarpState<NT>& st, int g, int t,
+                                            const VOffs& vo, const uint32_t (&eb)[8]) {
   const uint32_t tailmask = vr < kP ? (0xFFFFu & ~((1u << vr) - 1u)) : 0u;
 
   // ---- S^T = K . Q^T
   uint32_t kw[2][16];
-  if constexpr (COMP) load_k_comp(s, g, t, kw); else load_k_bf16(s, g, t, kw);
+  if constexpr (COMP) load_k_comp<KKILL>(s, g, t, kw); else load_k_bf16(s, g, t, kw);
   if constexpr (MODE == kGeneral) {
     const uint32_t fl = (COMP ? pm.rm[0] : 0u) | tailmask;
     if (fl != 0u) fix_k_rows(fl, pm.rm[0], pm.src[0], a.status, vr, g, t, kw);
@@ -493,57 +639,90 @@ __device__ __forceinline__ void attend_page(const Slot& s, const PageMeta& pm, i
 
   // ---- V fragments (issued before the softmax so the shared loads overlap it)
   uint32_t vw[2][8][2];
-  if constexpr (COMP) load_v_comp<MODE == kGeneral>(s, g, t, vw); else load_v_bf16(s, g, t, vw);
-  if constexpr (MODE == kGeneral) {
-    const uint32_t fl = (COMP ? pm.rm[1] : 0u) | tailmask;
-    if (fl != 0u) fix_v_rows(fl, pm.rm[1], pm.src[1], a.status, vr, g, t, vw);
-  } else if constexpr (MODE == kStaged && COMP) {
-    patch_v_staged<kRawArea>(pm.rm[1], pm.tag[1], pm.area, g, t, vw);
+  if constexpr (COMP && !EXK_V_LDSM) {
+    load_v_comp_lds<MODE == kGeneral>(s, g, t, vw);
+    if constexpr (MODE == kGeneral) {
+      const uint32_t fl = pm.rm[1] | tailmask;
+      if (fl != 0u) fix_v_rows(fl, pm.rm[1], pm.src[1], a.status, vr, g, t, vw);
+    } else if constexpr (MODE == kStaged) {
+      patch_v_staged<kRawArea>(pm.rm[1], pm.tag[1], pm.area, g, t, vw);
+    }
+  } else if constexpr (COMP) {
+    load_v_comp<MODE == kGeneral>(s, vo, eb, vw);
+    if constexpr (MODE == kGeneral) {
+      const uint32_t fl = pm.rm[1] | tailmask;
+      if (fl != 0u) fix_v_rows_t(fl, pm.rm[1], pm.src[1], a.status, vr, g, t, vw);
+    } else if constexpr (MODE == kStaged) {
+      patch_v_staged_t<kRawArea>(pm.rm[1], pm.tag[1], pm.area, g, t, vw);
+    }
+  } else {
+    load_v_bf16(s, g, t, vw);
+    if constexpr (MODE == kGeneral) {
+      if (tailmask != 0u) fix_v_rows(tailmask, 0u, pm.src[1], a.status, vr, g, t, vw);
+    }
   }
 
   // ---- online softmax (base 2) over the page's 16 rows
   const int r0 = sigma(g), r1 = r0 + 8;
   uint32_t pb[NT][2];
   float alpha[NT][2];
+  float p[NT][4];
+  bool grew = false;
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
-    float p[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) p[i] = sc[nt][i] * a.qk_scale;
+    for (int i = 0; i < 4; ++i) p[nt][i] = sc[nt][i] * a.qk_scale;
     if constexpr (MODE == kGeneral) {
-      if (r0 >= vr) p[0] = p[1] = -INFINITY;
-      if (r1 >= vr) p[2] = p[3] = -INFINITY;
+      if (r0 >= vr) p[nt][0] = p[nt][1] = -INFINITY;
+      if (r1 >= vr) p[nt][2] = p[nt][3] = -INFINITY;
     }
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
-      float mx = fmaxf(p[j], p[2 + j]);
+      float mx = fmaxf(p[nt][j], p[nt][2 + j]);
       mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 4));
       mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 8));
       mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 16));
       const float mn = fmaxf(st.m[nt][j], mx);
-      alpha[nt][j] = ex2(st.m[nt][j] - mn);
-      p[j] = ex2(p[j] - mn);
-      p[2 + j] = ex2(p[2 + j] - mn);
-      st.l[nt][j] = st.l[nt][j] * alpha[nt][j] + p[j] + p[2 + j];
-      st.m[nt][j] = mn;
+      grew |= mn != st.m[nt][j];
+      alpha[nt][j] = mn;  // the new maximum until the rescale decision
     }
-    // P (rows = tokens, cols = heads) -> P^T fragments via 8x8 transposes
-    pb[nt][0] = movmatrix_t(pack_bf16x2(p[0], p[1]));
-    pb[nt][1] = movmatrix_t(pack_bf16x2(p[2], p[3]));
   }
-
-  // ---- O^T = O^T * alpha + V^T . P^T
+  const bool rescale = EXK_LAZY_RESCALE ? __any_sync(0xFFFFFFFFu, grew) : true;
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
-    for (int mm = 0; mm < 8; ++mm) {
-      float* c = st.acc[nt][mm];
-      c[0] *= alpha[nt][0];
-      c[1] *= alpha[nt][1];
-      c[2] *= alpha[nt][0];
-      c[3] *= alpha[nt][1];
-      mma_bf16(st.acc[nt][mm], vw[0][mm][0], vw[0][mm][1], vw[1][mm][0], vw[1][mm][1], pb[nt][0], pb[nt][1]);
+    for (int j = 0; j < 2; ++j) {
+      const float mn = alpha[nt][j];
+      alpha[nt][j] = rescale ? ex2(st.m[nt][j] - mn) : 1.0f;
+      p[nt][j] = ex2(p[nt][j] - mn);
+      p[nt][2 + j] = ex2(p[nt][2 + j] - mn);
+      st.l[nt][j] = st.l[nt][j] * alpha[nt][j] + p[nt][j] + p[nt][2 + j];
+      st.m[nt][j] = mn;
     }
+    // P (rows = tokens, cols = heads) -> P^T fragments via 8x8 transposes
+    pb[nt][0] = movmatrix_t(pack_bf16x2(p[nt][0], p[nt][1]));
+    pb[nt][1] = movmatrix_t(pack_bf16x2(p[nt][2], p[nt][3]));
+  }
+
+  // ---- O^T = O^T * alpha + V^T . P^T
+  if (rescale) {
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+      for (int mm = 0; mm < 8; ++mm) {
+        float* c = st.acc[nt][mm];
+        c[0] *= alpha[nt][0];
+        c[1] *= alpha[nt][1];
+        c[2] *= alpha[nt][0];
+        c[3] *= alpha[nt][1];
+      }
+    }
+  }
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+    for (int mm = 0; mm < 8; ++mm)
+      mma_bf16(st.acc[nt][mm], vw[0][mm][0], vw[0][mm][1], vw[1][mm][0], vw[1][mm][1], pb[nt][0], pb[nt][1]);
   }
 }
 
@@ -987,6 +1166,7 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
   // -------------------------------------------------- consumers: warp = (head hl, page phase ph)
   const int g = lane >> 2, t = lane & 3;
   const int hl = warp / WPH, ph = warp % WPH;
+  const VOffs vo = v_offsets(lane);
   uint32_t gs = 0;
   bool aborted = false;
   WarpState<NT> st;
@@ -1030,16 +1210,31 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
           const Slot tl = tile_ptrs<COMP, NWC, HG>(ring + slot * C::kStageBytes, hl, ph);
           // warp-uniform choice of the page body
           bool vzero = false;
+#if EXK_KZERO_BRANCH
+          bool kzero = true;
+#endif
+          uint32_t eb[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
           if constexpr (COMP) {
-            const uint2 bl = *reinterpret_cast<const uint2*>(tl.p[5] + 8 * g);
-            const uint2 bh = *reinterpret_cast<const uint2*>(tl.p[5] + 64 + 8 * g);
-            vzero = __any_sync(0xFFFFFFFFu, ((bl.x | bl.y | bh.x | bh.y) & 0x80808080u) != 0u);
+            load_v_base(tl, vo, eb);
+            vzero = __any_sync(0xFFFFFFFFu, ((eb[0] | eb[1] | eb[2] | eb[3] | eb[4] | eb[5] | eb[6] | eb[7]) &
+                                             0x80808080u) != 0u);
+#if EXK_KZERO_BRANCH
+            const uint4 kl = *reinterpret_cast<const uint4*>(tl.p[2] + 16 * t);
+            const uint4 kh = *reinterpret_cast<const uint4*>(tl.p[2] + 64 + 16 * t);
+            kzero = __any_sync(0xFFFFFFFFu, ((kl.x | kl.y | kl.z | kl.w | kh.x | kh.y | kh.z | kh.w) &
+                                             0x80808080u) != 0u);
+#endif
           }
           if ((pm.rm[0] | pm.rm[1]) == 0u && vr == kP && !vzero) {
-            attend_page<COMP, NT, kFast>(tl, pm, vr, a, qf, st, g, t);
+#if EXK_KZERO_BRANCH
+            if (!kzero)
+              attend_page<COMP, NT, kFast, false>(tl, pm, vr, a, qf, st, g, t, vo, eb);
+            else
+#endif
+              attend_page<COMP, NT, kFast, true>(tl, pm, vr, a, qf, st, g, t, vo, eb);
           } else if (COMP && vr == kP && !vzero && (pm.rm[0] == 0u || pm.tag[0] != 0xFFu) &&
                      (pm.rm[1] == 0u || pm.tag[1] != 0xFFu)) {
-            attend_page<COMP, NT, kStaged>(tl, pm, vr, a, qf, st, g, t);
+            attend_page<COMP, NT, kStaged, true>(tl, pm, vr, a, qf, st, g, t, vo, eb);
           } else {
 #pragma unroll
             for (int kv = 0; kv < 2; ++kv) {
@@ -1055,7 +1250,7 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
                 pm.src[kv].lim = a.raw_rows[kv] - ro < kP ? static_cast<int>(a.raw_rows[kv] - ro) : kP;
               }
             }
-            attend_page<COMP, NT, kGeneral>(tl, pm, vr, a, qf, st, g, t);
+            attend_page<COMP, NT, kGeneral, true>(tl, pm, vr, a, qf, st, g, t, vo, eb);
           }
         }
         __syncwarp();
@@ -1090,7 +1285,7 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
             }
 #pragma unroll
             for (int mm = 0; mm < 8; ++mm) {
-              const int chA = mm < 4 ? 8 * g + 2 * mm : 64 + 8 * g + 2 * (mm - 4);
+              const int chA = v_channel<COMP>(mm, g);
               *reinterpret_cast<float2*>(a.ws_o + col * kD + chA) = make_float2(st.acc[nt][mm][j], st.acc[nt][mm][2 + j]);
             }
           }
@@ -1137,7 +1332,7 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
           for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
             for (int mm = 0; mm < 8; ++mm) {
-              const int chA = mm < 4 ? 8 * g + 2 * mm : 64 + 8 * g + 2 * (mm - 4);
+              const int chA = v_channel<COMP>(mm, g);
 #pragma unroll
               for (int j = 0; j < 2; ++j) {
                 float* r = buf + (nt * 8 + 2 * t + j) * kAccPitch + chA;

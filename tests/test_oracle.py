@@ -109,3 +109,25 @@ def test_oracle_two_level_merge(case):
     ge = oatt.merge_group(np.where(np.isneginf(m2)[..., None], 0, o), m2, np.where(np.isneginf(m2), 0, l))
     gd = oatt.merge_group(np.delete(o, 5, 1), np.delete(m, 5, 1), np.delete(l, 5, 1))
     assert all(np.array_equal(a, b) for a, b in zip(ge, gd))
+
+
+def test_torch_attention_restatement_matches_the_numpy_oracle():
+    """bench.py's CPU baseline states the reference attention in torch
+    (oracle/torch_attention.py); it agrees with the numpy oracle within the
+    stated tolerance, partial last pages and several splits included."""
+    import torch
+
+    from oracle import torch_attention
+    rng = np.random.default_rng(5)
+    for B, T, Hq, Hkv in [(2, 1000, 8, 2), (1, 777, 28, 4), (3, 100, 16, 2)]:
+        TS = -(-T // 16) * 16
+        k = (rng.standard_normal((B, TS, Hkv, 128)) * np.exp(rng.standard_normal((Hkv, 128)))).astype(np.float32)
+        v = rng.standard_normal((B, TS, Hkv, 128)).astype(np.float32)
+        q = rng.standard_normal((B, Hq, 128)).astype(np.float32)
+        kb, vb, qb = (f32_to_bits(x) for x in (k, v, q))
+        tk = lambda b: torch.from_numpy(b.view(np.int16).copy()).view(torch.bfloat16)  # noqa: E731
+        got = torch_attention.attention(tk(qb), tk(kb), tk(vb), T)
+        got = bits_to_f32(got.view(torch.int16).numpy().view(np.uint16)).astype(np.float64)
+        want = bits_to_f32(oatt.attention(qb, kb, vb, T)).astype(np.float64)
+        tol = oatt.tolerance(qb, kb, vb, T, want)
+        assert (np.abs(got - want) <= tol).all(), (B, T, Hq, Hkv)
