@@ -100,7 +100,9 @@ def parse_args():
     ap.add_argument("--no-engine", action="store_true")
     ap.add_argument("--no-kv-split", action="store_true")
     ap.add_argument("--no-configs", action="store_true")
-    ap.add_argument("--engine-steps", type=int, default=24)
+    ap.add_argument("--engine-gen", type=int, default=256, help="tokens generated per engine run")
+    ap.add_argument("--engine-real-prompts", type=int, default=16,
+                    help="sequences per engine prefilled from random-id prompts through the model")
     ap.add_argument("--num-warps", type=int, default=8)
     ap.add_argument("--record-traffic", metavar="NCU_REP",
                     help="write the split kernel's per-launch DRAM bytes from an ncu report and exit")
@@ -875,35 +877,40 @@ def run_kv_split(a, dev, rank, world, T=131072, Hq=32, Hkv=8, reps=20):
                     "group partials and the gathered merge"}
 
 
-def run_engine(a, dev, world, context=4096, warm=4):
-    """Engine decode tok/s on a random-init Llama-3.1-8B (see the module docstring)."""
-    import gc
+def _engine_model(dev):
     import torch
-    import torch.distributed as dist
     from transformers import LlamaConfig, LlamaForCausalLM
-
-    import exactkv_b200 as ekv
-    from exactkv_b200 import synthetic
-
-    gc.collect()
-    torch.cuda.empty_cache()
     cfg = LlamaConfig(vocab_size=128256, hidden_size=4096, intermediate_size=14336, num_hidden_layers=32,
                       num_attention_heads=32, num_key_value_heads=8, head_dim=128, rope_theta=5e5,
                       max_position_embeddings=8192, rms_norm_eps=1e-5, initializer_range=0.02,
                       tie_word_embeddings=False)
     torch.manual_seed(1234)
     with torch.device(dev):
-        model = LlamaForCausalLM._from_config(cfg, dtype=torch.bfloat16).eval()
-    steps = a.engine_steps
-    TM = context + warm + steps + 16
-    per_seq = ekv.Engine(model, 2, TM).kv_bytes() - ekv.Engine(model, 1, TM).kv_bytes()
-    torch.cuda.empty_cache()
+        return LlamaForCausalLM._from_config(cfg, dtype=torch.bfloat16).eval()
+
+
+def _engine_run(model, backend, B, context, gen, warm, real, dev, world):
+    """One engine at batch B: `real` sequences prefilled from uniform-random-id
+    prompts of `context` tokens through Engine.prefill (the model's forward pass),
+    the rest from the synthetic KV through the prefill encoder; then `gen` greedy
+    tokens, the last gen - warm timed with CUDA events. Also the 32 layers'
+    decode-attention calls of one step, timed alone at the end."""
+    import torch
+    import torch.distributed as dist
+
+    import exactkv_b200 as ekv
+    from exactkv_b200 import kernels, synthetic
+    eng = ekv.Engine(model, B, context + gen + 16, backend=backend)
+    g = torch.Generator(device=dev).manual_seed(77)
+    ids = torch.randint(0, model.config.vocab_size, (real, context), generator=g, device=dev)
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    tok = torch.empty(B, dtype=torch.long, device=dev)
+    tok[:real] = eng.prefill(ids)
+    torch.cuda.synchronize(dev)
+    prefill_s = time.perf_counter() - t0
     chunk = 16
-    scratch = 2 * chunk * context * 8 * 128 * 2 * 2           # the synthetic K/V chunk (and its copy)
-    budget = torch.cuda.mem_get_info(dev)[0] - int(1.6 * 2 ** 30) - scratch - (2 << 30)   # 2 GiB for activations
-    B = max(1, min(1024, budget // per_seq))
-    eng = ekv.Engine(model, B, TM)
-    for b0 in range(0, B, chunk):
+    for b0 in range(real, B, chunk):
         n = min(chunk, B - b0)
         k = synthetic.make_kv(n, context, 8, seed=900 + b0, theta=5e5, key=True, device=dev)
         v = synthetic.make_kv(n, context, 8, seed=901 + b0, theta=5e5, key=False, device=dev)
@@ -912,17 +919,18 @@ def run_engine(a, dev, world, context=4096, warm=4):
                 kc.prefill_slot(b0 + j, k[j:j + 1])
                 vc.prefill_slot(b0 + j, v[j:j + 1])
         del k, v
-    tok = torch.randint(0, cfg.vocab_size, (B,), device=dev)
+    tok[real:] = torch.randint(0, model.config.vocab_size, (B - real,), generator=g, device=dev)
+    eng.sync_length()
     for _ in range(warm):
-        tok = eng.step(tok).argmax(-1)
+        tok = eng.step_greedy(tok)
     stream = torch.cuda.current_stream(dev)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(steps):
-        tok = eng.step(tok).argmax(-1)
+    for _ in range(gen - warm):
+        tok = eng.step_greedy(tok)
     e1.record(stream)
     torch.cuda.synchronize(dev)
     ms = e0.elapsed_time(e1)
@@ -930,12 +938,81 @@ def run_engine(a, dev, world, context=4096, warm=4):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
-    res = {"tok_s": round(B * steps * world / (ms * 1e-3), 1), "batch_per_gpu": int(B), "context": context,
-           "steps": steps, "ms_per_step": round(ms / steps, 3), "kv_mib_per_seq": round(per_seq / 2 ** 20, 1),
-           "pool_grows": int(eng.grows), "model": "random-init Llama-3.1-8B (bf16)",
-           "what": "greedy decode steps through exactkv_b200.Engine (HF modules + compressed caches), "
-                   "contexts filled with the synthetic KV"}
-    del eng, model
+    steps = gen - warm
+    # the attention share of a step: the 32 layers' decode-attention calls alone,
+    # on the same caches at the final length (after the graph's last step)
+    q = synthetic.make_q(B, 32, seed=5, device=dev)
+    length = torch.full((1,), eng.T - 1, dtype=torch.int32, device=dev)
+    def attn_calls():
+        for kc, vc in eng.kv:
+            if eng.compressed:
+                kernels.attention_compressed_devlen(q, kc, vc, length, 1)
+            else:
+                kernels.attention_reference_devlen(q, kc.buf, vc.buf, length, 1)
+    attn_calls()
+    torch.cuda.synchronize(dev)
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record(stream)
+    for _ in range(5):
+        attn_calls()
+    a1.record(stream)
+    torch.cuda.synchronize(dev)
+    attn_ms = a0.elapsed_time(a1) / 5
+    res = {"backend": backend, "batch_per_gpu": int(B), "tok_s": round(B * steps * world / (ms * 1e-3), 1),
+           "ms_per_step": round(ms / steps, 3), "attn_ms_per_step": round(attn_ms, 3),
+           "attn_share": round(attn_ms / (ms / steps), 3), "prefill_s_real_prompts": round(prefill_s, 2),
+           "pool_grows": int(eng.grows), "graph_captures": int(eng.captures)}
+    eng.close()
+    del eng
+    return res
+
+
+def run_engine(a, dev, world, context=4096, warm=4):
+    """BASELINE configs[4] on each GPU: the bf16-cache engine and the compressed
+    engine, each at the batch that fills the KV budget (free HBM minus 1.6 GiB and
+    the activations), then the compressed engine at the bf16 batch (the
+    reference's own E2E comparison, bench/e2e.py:52-90 of the reference)."""
+    import gc
+    import torch
+
+    import exactkv_b200 as ekv
+
+    gc.collect()
+    torch.cuda.empty_cache()
+    model = _engine_model(dev)
+    gen = a.engine_gen
+    TM = context + gen + 16
+    per_seq = {}
+    for be in ("bf16", "exactkv"):
+        e1, e2 = ekv.Engine(model, 1, TM, backend=be), ekv.Engine(model, 2, TM, backend=be)
+        per_seq[be] = e2.kv_bytes() - e1.kv_bytes()
+        del e1, e2
+        torch.cuda.empty_cache()
+    chunk = 16
+    scratch = 2 * chunk * context * 8 * 128 * 2 * 2           # the synthetic K/V chunk (and its copy)
+    budget = torch.cuda.mem_get_info(dev)[0] - int(1.6 * 2 ** 30) - scratch - (3 << 30)   # activations, graph
+    rows = []
+    for be in ("bf16", "exactkv"):
+        B = max(1, min(2048, budget // per_seq[be]))
+        rows.append(_engine_run(model, be, B, context, gen, warm, min(a.engine_real_prompts, B), dev, world))
+        gc.collect()
+        torch.cuda.empty_cache()
+    same = _engine_run(model, "exactkv", rows[0]["batch_per_gpu"], context, gen, warm,
+                       min(a.engine_real_prompts, rows[0]["batch_per_gpu"]), dev, world)
+    res = {"tok_s_exactkv": rows[1]["tok_s"], "tok_s_bf16": rows[0]["tok_s"],
+           "throughput_ratio": round(rows[1]["tok_s"] / rows[0]["tok_s"], 3),
+           "batch_exactkv": rows[1]["batch_per_gpu"], "batch_bf16": rows[0]["batch_per_gpu"],
+           "step_time_ratio_same_batch": round(rows[0]["ms_per_step"] / same["ms_per_step"], 3),
+           "attn_share_exactkv": rows[1]["attn_share"], "attn_share_bf16": rows[0]["attn_share"],
+           "kv_mib_per_seq": {be: round(v / 2 ** 20, 1) for be, v in per_seq.items()},
+           "kv_budget_gib": round(budget / 2 ** 30, 2), "context": context, "generated": gen,
+           "timed_steps": gen - warm, "rows": rows + [same],
+           "model": "random-init Llama-3.1-8B (bf16 weights ~ N(0, 0.02))",
+           "what": f"greedy decode through exactkv_b200.Engine (HF modules, CUDA-graphed step). Per engine: "
+                   f"{a.engine_real_prompts} sequences prefilled from {context}-token uniform-random-id prompts "
+                   f"through Engine.prefill (model forward), the rest of the batch from the synthetic KV "
+                   f"through the prefill encoder; {gen} generated tokens, the last {gen - warm} timed"}
+    del model
     gc.collect()
     torch.cuda.empty_cache()
     return res

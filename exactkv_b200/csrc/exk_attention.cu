@@ -242,48 +242,6 @@ __device__ __forceinline__ void load_k_bf16(const Slot& s, int g, int t, uint32_
   }
 }
 
-// The V loader without ldmatrix (EXK_V_LDSM = 0): per-lane 8-byte loads and a
-// byte interleave of the two tokens of a pair; channel map 8g + 2mm.
-template <bool VKILL>
-__device__ __forceinline__ void load_v_comp_lds(const Slot& s, int g, int t, uint32_t (&vw)[2][8][2]) {
-  const uint8_t* sm = s.p[3];
-  const uint8_t* cd = s.p[4];
-  const uint8_t* bs = s.p[5];
-  const uint2 bl = *reinterpret_cast<const uint2*>(bs + 8 * g);
-  const uint2 bh = *reinterpret_cast<const uint2*>(bs + 64 + 8 * g);
-  // base bytes duplicated per token pair: [b(c), b(c), b(c+1), b(c+1)]
-  const uint32_t eb[8] = {prmt(bl.x, bl.x, 0x1100u), prmt(bl.x, bl.x, 0x3322u), prmt(bl.y, bl.y, 0x1100u),
-                          prmt(bl.y, bl.y, 0x3322u), prmt(bh.x, bh.x, 0x1100u), prmt(bh.x, bh.x, 0x3322u),
-                          prmt(bh.y, bh.y, 0x1100u), prmt(bh.y, bh.y, 0x3322u)};
-  const int ch = g >> 1, half = (g & 1) * 8;
-#pragma unroll
-  for (int pp = 0; pp < 2; ++pp) {
-    const int ra = sigma(2 * t) + 8 * pp;
-    const int rb = sigma(2 * t + 1) + 8 * pp;
-    const uint2 al = *reinterpret_cast<const uint2*>(sm + ra * 128 + ((ch ^ (ra & 7)) << 4) + half);
-    const uint2 ah = *reinterpret_cast<const uint2*>(sm + ra * 128 + (((ch + 4) ^ (ra & 7)) << 4) + half);
-    const uint2 ac = *reinterpret_cast<const uint2*>(cd + ra * 64 + ((ch ^ ((ra >> 1) & 3)) << 4) + half);
-    const uint2 bl2 = *reinterpret_cast<const uint2*>(sm + rb * 128 + ((ch ^ (rb & 7)) << 4) + half);
-    const uint2 bh2 = *reinterpret_cast<const uint2*>(sm + rb * 128 + (((ch + 4) ^ (rb & 7)) << 4) + half);
-    const uint2 bc = *reinterpret_cast<const uint2*>(cd + rb * 64 + ((ch ^ ((rb >> 1) & 3)) << 4) + half);
-    // interleave the two tokens' bytes: [A(c), B(c), A(c+1), B(c+1)]
-    const uint32_t il[4] = {prmt(al.x, bl2.x, 0x5140u), prmt(al.x, bl2.x, 0x7362u), prmt(al.y, bl2.y, 0x5140u),
-                            prmt(al.y, bl2.y, 0x7362u)};
-    const uint32_t ih[4] = {prmt(ah.x, bh2.x, 0x5140u), prmt(ah.x, bh2.x, 0x7362u), prmt(ah.y, bh2.y, 0x5140u),
-                            prmt(ah.y, bh2.y, 0x7362u)};
-    const uint32_t jc[4] = {prmt(ac.x, bc.x, 0x5140u), prmt(ac.x, bc.x, 0x7362u), prmt(ac.y, bc.y, 0x5140u),
-                            prmt(ac.y, bc.y, 0x7362u)};
-#pragma unroll
-    for (int mm = 0; mm < 4; ++mm)
-      dec4<VKILL>(il[mm], lo_nibbles(jc[mm]), VKILL ? eb[mm] & 0x7F7F7F7Fu : eb[mm], eb[mm], vw[pp][mm][0],
-                  vw[pp][mm][1]);
-#pragma unroll
-    for (int mm = 4; mm < 8; ++mm)
-      dec4<VKILL>(ih[mm - 4], hi_nibbles(jc[mm - 4]), VKILL ? eb[mm] & 0x7F7F7F7Fu : eb[mm], eb[mm], vw[pp][mm][0],
-                  vw[pp][mm][1]);
-  }
-}
-
 // Compressed V through ldmatrix.trans. The bytes of the sm and code tiles are
 // read as b16 elements (two channels each), so a transposed 8x8 load gives lane
 // (g, t) the word [A(ch), A(ch+1), B(ch), B(ch+1)] of tokens A, B (the matrix
@@ -319,12 +277,9 @@ __device__ __forceinline__ VOffs v_offsets(int lane) {
 }
 
 // Channel of row g of V m-tile c (row g + 8 holds the next channel).
-#ifndef EXK_V_LDSM
-#define EXK_V_LDSM 1
-#endif
 template <bool COMP>
 __device__ __forceinline__ int v_channel(int c, int g) {
-  if constexpr (COMP && EXK_V_LDSM) return 16 * c + 2 * g;
+  if constexpr (COMP) return 16 * c + 2 * g;
   return c < 4 ? 8 * g + 2 * c : 64 + 8 * g + 2 * (c - 4);
 }
 
@@ -537,37 +492,6 @@ __device__ __forceinline__ void patch_k_staged(uint32_t rm, uint32_t tag, const 
 }
 
 template <int R>
-__device__ __forceinline__ void patch_v_staged(uint32_t rm, uint32_t tag, const uint16_t* area, int g, int t,
-                                               uint32_t (&vw)[2][8][2]) {
-#pragma unroll
-  for (int pp = 0; pp < 2; ++pp) {
-    const int ra = sigma(2 * t) + 8 * pp;
-    const int rb = sigma(2 * t + 1) + 8 * pp;
-    const bool fa = (rm >> ra) & 1u, fb = (rm >> rb) & 1u;
-    if (fa || fb) {
-      uint32_t wa[8], wb[8];
-#pragma unroll
-      for (int ab = 0; ab < 2; ++ab) {
-        const int r = ab ? rb : ra;
-        uint32_t* w = ab ? wb : wa;
-        const uint4* row = staged_row<R>(area, tag, rm, r);
-        const bool f = ab ? fb : fa;
-        const uint4 x = f ? row[g] : make_uint4(0, 0, 0, 0), y = f ? row[8 + g] : make_uint4(0, 0, 0, 0);
-        w[0] = x.x; w[1] = x.y; w[2] = x.z; w[3] = x.w; w[4] = y.x; w[5] = y.y; w[6] = y.z; w[7] = y.w;
-      }
-      const uint32_t mask = (fa ? 0x0000FFFFu : 0u) | (fb ? 0xFFFF0000u : 0u);
-#pragma unroll
-      for (int mm = 0; mm < 8; ++mm) {
-        const uint32_t n0 = prmt(wa[mm], wb[mm], 0x5410u);
-        const uint32_t n1 = prmt(wa[mm], wb[mm], 0x7632u);
-        vw[pp][mm][0] = (vw[pp][mm][0] & ~mask) | (n0 & mask);
-        vw[pp][mm][1] = (vw[pp][mm][1] & ~mask) | (n1 & mask);
-      }
-    }
-  }
-}
-
-template <int R>
 __device__ __forceinline__ void patch_v_staged_t(uint32_t rm, uint32_t tag, const uint16_t* area, int g, int t,
                                                  uint32_t (&vw)[2][8][2]) {
 #pragma unroll
@@ -595,16 +519,19 @@ enum PageMode { kFast = 0, kStaged = 1, kGeneral = 2 };
 // alpha = 1 exactly (ex2(0) = 1) the skipped multiplies would leave every bit as
 // it is, so the result is the same either way. EXK_LAZY_RESCALE = 0 restores the
 // unconditional rescale.
+// 1: each consumer warp prefetches the next item's query rows into L2.
+#ifndef EXK_Q_PREFETCH
+#define EXK_Q_PREFETCH 1
+#endif
+
 #ifndef EXK_LAZY_RESCALE
 #define EXK_LAZY_RESCALE 1
 #endif
-// 1: pages whose K holds no zero group take a K decoder without the code-0 rule
-// (one more copy of the fast body).
-#ifndef EXK_KZERO_BRANCH
-#define EXK_KZERO_BRANCH 0
-#endif
 
-// KKILL: the page's K holds a zero group (compressed kernel; else ignored).
+
+// KKILL = false would skip K's code-0 rule on pages without a K zero group;
+// every body keeps it (a second fast body for such pages measured 121 vs 90 us
+// at 32x4096: the larger loop schedules worse).
 template <bool COMP, int NT, int MODE, bool KKILL>
 __device__ __forceinline__ void attend_page(const Slot& s, const PageMeta& pm, int vr, const AttnArgs& a,
                                             const uint32_t (&qf)[NT][16], WarpState<NT>& st, int g, int t,
@@ -639,15 +566,7 @@ __device__ __forceinline__ void attend_page(const Slot& s, const PageMeta& pm, i
 
   // ---- V fragments (issued before the softmax so the shared loads overlap it)
   uint32_t vw[2][8][2];
-  if constexpr (COMP && !EXK_V_LDSM) {
-    load_v_comp_lds<MODE == kGeneral>(s, g, t, vw);
-    if constexpr (MODE == kGeneral) {
-      const uint32_t fl = pm.rm[1] | tailmask;
-      if (fl != 0u) fix_v_rows(fl, pm.rm[1], pm.src[1], a.status, vr, g, t, vw);
-    } else if constexpr (MODE == kStaged) {
-      patch_v_staged<kRawArea>(pm.rm[1], pm.tag[1], pm.area, g, t, vw);
-    }
-  } else if constexpr (COMP) {
+  if constexpr (COMP) {
     load_v_comp<MODE == kGeneral>(s, vo, eb, vw);
     if constexpr (MODE == kGeneral) {
       const uint32_t fl = pm.rm[1] | tailmask;
@@ -1177,6 +1096,16 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
     const int hk = it.hg * HG + hl;
     const int nst = (it.npages + WPH - 1) / WPH;
     load_q<NT>(a, it.b, hk, g, t, qf);
+#if EXK_Q_PREFETCH
+    // the next item's queries, fetched into L2 while this item streams (its
+    // first load then waits for L2, not DRAM, while the ring sits full)
+    if (item + static_cast<int>(gridDim.x) < a.n_items) {
+      const Item nx = decode_item(a, item + gridDim.x);
+      const char* qn = reinterpret_cast<const char*>(
+          a.q + (static_cast<int64_t>(nx.b) * a.Hq + static_cast<int64_t>(nx.hg * HG + hl) * a.G) * kD);
+      if (lane * 128 < a.G * kD * 2) prefetch_l2(qn + lane * 128);
+    }
+#endif
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       st.m[nt][0] = st.m[nt][1] = -INFINITY;
@@ -1210,28 +1139,14 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
           const Slot tl = tile_ptrs<COMP, NWC, HG>(ring + slot * C::kStageBytes, hl, ph);
           // warp-uniform choice of the page body
           bool vzero = false;
-#if EXK_KZERO_BRANCH
-          bool kzero = true;
-#endif
           uint32_t eb[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
           if constexpr (COMP) {
             load_v_base(tl, vo, eb);
             vzero = __any_sync(0xFFFFFFFFu, ((eb[0] | eb[1] | eb[2] | eb[3] | eb[4] | eb[5] | eb[6] | eb[7]) &
                                              0x80808080u) != 0u);
-#if EXK_KZERO_BRANCH
-            const uint4 kl = *reinterpret_cast<const uint4*>(tl.p[2] + 16 * t);
-            const uint4 kh = *reinterpret_cast<const uint4*>(tl.p[2] + 64 + 16 * t);
-            kzero = __any_sync(0xFFFFFFFFu, ((kl.x | kl.y | kl.z | kl.w | kh.x | kh.y | kh.z | kh.w) &
-                                             0x80808080u) != 0u);
-#endif
           }
           if ((pm.rm[0] | pm.rm[1]) == 0u && vr == kP && !vzero) {
-#if EXK_KZERO_BRANCH
-            if (!kzero)
-              attend_page<COMP, NT, kFast, false>(tl, pm, vr, a, qf, st, g, t, vo, eb);
-            else
-#endif
-              attend_page<COMP, NT, kFast, true>(tl, pm, vr, a, qf, st, g, t, vo, eb);
+            attend_page<COMP, NT, kFast, true>(tl, pm, vr, a, qf, st, g, t, vo, eb);
           } else if (COMP && vr == kP && !vzero && (pm.rm[0] == 0u || pm.tag[0] != 0xFFu) &&
                      (pm.rm[1] == 0u || pm.tag[1] != 0xFFu)) {
             attend_page<COMP, NT, kStaged, true>(tl, pm, vr, a, qf, st, g, t, vo, eb);
