@@ -519,11 +519,6 @@ enum PageMode { kFast = 0, kStaged = 1, kGeneral = 2 };
 // alpha = 1 exactly (ex2(0) = 1) the skipped multiplies would leave every bit as
 // it is, so the result is the same either way. EXK_LAZY_RESCALE = 0 restores the
 // unconditional rescale.
-// 1: each consumer warp prefetches the next item's query rows into L2.
-#ifndef EXK_Q_PREFETCH
-#define EXK_Q_PREFETCH 1
-#endif
-
 #ifndef EXK_LAZY_RESCALE
 #define EXK_LAZY_RESCALE 1
 #endif
@@ -1096,16 +1091,6 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
     const int hk = it.hg * HG + hl;
     const int nst = (it.npages + WPH - 1) / WPH;
     load_q<NT>(a, it.b, hk, g, t, qf);
-#if EXK_Q_PREFETCH
-    // the next item's queries, fetched into L2 while this item streams (its
-    // first load then waits for L2, not DRAM, while the ring sits full)
-    if (item + static_cast<int>(gridDim.x) < a.n_items) {
-      const Item nx = decode_item(a, item + gridDim.x);
-      const char* qn = reinterpret_cast<const char*>(
-          a.q + (static_cast<int64_t>(nx.b) * a.Hq + static_cast<int64_t>(nx.hg * HG + hl) * a.G) * kD);
-      if (lane * 128 < a.G * kD * 2) prefetch_l2(qn + lane * 128);
-    }
-#endif
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       st.m[nt][0] = st.m[nt][1] = -INFINITY;
