@@ -51,13 +51,19 @@ decode on the same bf16 K/V (16-token pages), timed like our calls.
 
 kv_split: configs[3] (1 x 131072 split by KV sequence over the ranks).
 
-engine: BASELINE configs[4] decode throughput through exactkv_b200.Engine on a
-random-init Llama-3.1-8B (32 layers, hidden 4096, 32 q / 8 kv heads, FFN 14336,
-vocab 128256, bf16 weights ~ N(0, 0.02)), batch sized to the free HBM minus
-1.6 GiB (and the synthetic context's scratch); every sequence's 4096-token
-context is filled with the synthetic KV through the prefill encoder (the
-decode step's cost does not depend on how the context was produced), then
-greedy steps are timed with CUDA events; tok/s summed over ranks.
+engine: BASELINE configs[4] through exactkv_b200.Engine (CUDA-graphed decode
+step) on a random-init Llama-3.1-8B (32 layers, hidden 4096, 32 q / 8 kv heads,
+FFN 14336, vocab 128256, bf16 weights ~ N(0, 0.02)). The bf16-cache engine and
+the compressed engine each run at the batch that fills the KV budget (free HBM
+minus 1.6 GiB, the activations and the synthetic context's scratch), then the
+compressed engine at the bf16 batch — the reference's own E2E comparison
+(bench/e2e.py of the reference). Per engine, the first --engine-real-prompts
+sequences are prefilled from 4096-token uniform-random-id prompts through
+Engine.prefill (the model's forward pass) and the rest of the batch from the
+synthetic KV through the prefill encoder; then --engine-gen (256) greedy
+tokens, all but the first 4 timed with CUDA events; tok/s summed over ranks.
+attn_ms_per_step: the 32 layers' decode-attention calls of one step timed
+alone on the same caches, and attn_share its fraction of the step.
 
 --impl reference: the reference's own CPU path on the host cores — its PyTorch
 codec (exactkv.codec.decode_reference, loaded unmodified from baseline/_ref)
