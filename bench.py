@@ -172,8 +172,9 @@ def record_traffic(rep, batch, scale):
     mult = {"byte": 1, "Kbyte": 1e3, "Mbyte": 1e6, "Gbyte": 1e9}
     per_launch = []
     for r in rows[2:]:
-        if "attn_split_kernel" not in r[col["Kernel Name"]] or "ILb1" not in r[col["Kernel Name"]] and \
-                "<true" not in r[col["Kernel Name"]]:
+        name = r[col["Kernel Name"]]
+        # the compressed instantiation: <1, ...> demangled, ILb1 mangled, <true, ...> with bool names
+        if "attn_split_kernel" not in name or not any(k in name for k in ("<1,", "ILb1", "<true")):
             continue
         tot = 0.0
         for m in ("dram__bytes_read.sum", "dram__bytes_write.sum"):
