@@ -351,6 +351,7 @@ __global__ void __launch_bounds__(kEncWarps * 32) raw_copy_kernel(const __grid_c
 // (sequence, page, head) order as raw_offsets_kernel + raw_copy_kernel.
 constexpr int kChunkPh = 256;
 constexpr int kChunkThreads = 256;  // one page-head per thread
+constexpr int kCopyBatch = 8;       // raw rows a placement warp loads before storing them
 
 __device__ __forceinline__ int64_t prefill_page(const EncArgs& a, int ph) {
   int bi, pg, hk;
@@ -454,30 +455,69 @@ __global__ void __launch_bounds__(kChunkThreads) chunk_place_kernel(const __grid
     off += __popc(rm[j]);
   }
   __syncthreads();
-  // each warp copies the raw rows of its share of the chunk, a row per step
+  // each warp copies the raw rows of its share of the chunk. The sources are
+  // cold (the encode pass read them long ago), so the warp queues up to
+  // kCopyBatch rows — across page-heads — and loads them all before storing.
+  __shared__ int64_t s_src[kChunkThreads / 32][kCopyBatch];
+  __shared__ int64_t s_dst[kChunkThreads / 32][kCopyBatch];
+  int n = 0;
+  auto flush = [&]() {
+    __syncwarp();
+    uint32_t v[kCopyBatch][2];
+#pragma unroll
+    for (int j = 0; j < kCopyBatch; ++j) {
+      v[j][0] = v[j][1] = 0u;
+      if (j < n) {
+        const uint16_t* src = a.src + s_src[warp][j];
+        if constexpr (VEC) {
+          const uint2 x = reinterpret_cast<const uint2*>(src)[lane];
+          v[j][0] = x.x;
+          v[j][1] = x.y;
+        } else {
+          v[j][0] = src[4 * lane] | (uint32_t(src[4 * lane + 1]) << 16);
+          v[j][1] = src[4 * lane + 2] | (uint32_t(src[4 * lane + 3]) << 16);
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kCopyBatch; ++j) {
+      if (j < n) {
+        uint16_t* d = a.raw + s_dst[warp][j] * kD;
+        if constexpr (VEC) {
+          reinterpret_cast<uint2*>(d)[lane] = make_uint2(v[j][0], v[j][1]);
+        } else {
+          d[4 * lane] = static_cast<uint16_t>(v[j][0]);
+          d[4 * lane + 1] = static_cast<uint16_t>(v[j][0] >> 16);
+          d[4 * lane + 2] = static_cast<uint16_t>(v[j][1]);
+          d[4 * lane + 3] = static_cast<uint16_t>(v[j][1] >> 16);
+        }
+      }
+    }
+    __syncwarp();
+    n = 0;
+  };
   for (int i = warp; i < kChunkPh; i += kChunkThreads / 32) {
     uint32_t m = s_rm[i];
     if (m == 0u) continue;
     const int ph = c0 + i;
     int bi, pg, hk;
     page_index(a, a.pg0, ph, bi, pg, hk);
+    const int64_t src0 = bi * a.s_b + pg * a.s_pg + hk * a.s_h;
     int64_t ridx = s_off[i];
     while (m != 0u) {
       const int tok = __ffs(m) - 1;
       m &= m - 1u;
       if (ridx >= 0 && ridx < a.raw_cap) {
-        const uint16_t* src = a.src + bi * a.s_b + pg * a.s_pg + static_cast<int64_t>(tok) * a.s_p + hk * a.s_h;
-        uint16_t* d = a.raw + ridx * kD;
-        if constexpr (VEC) {
-          reinterpret_cast<uint2*>(d)[lane] = reinterpret_cast<const uint2*>(src)[lane];
-        } else {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) d[4 * lane + j] = src[4 * lane + j];
+        if (lane == 0) {
+          s_src[warp][n] = src0 + static_cast<int64_t>(tok) * a.s_p;
+          s_dst[warp][n] = ridx;
         }
+        if (++n == kCopyBatch) flush();
       }
       ++ridx;
     }
   }
+  if (n > 0) flush();
 }
 
 struct DecArgs {
