@@ -367,7 +367,7 @@ def run_ours(a, rank, world, local):
     del k, v
     kernels.check_status(dev)
 
-    ns, sl = kernels.plan_splits(B, Hkv, T, dev)
+    ns, sl = kernels.call_plan(B, Hkv, T, dev, a.num_warps)   # the plan decode_attention uses
     stream = torch.cuda.current_stream(dev)
     nbytes, raw_rows = algorithmic_bytes(kc, vc, B, Hkv, Hq, T, ns)
     bf16_bytes = 2 * B * T * Hkv * 256
@@ -736,7 +736,7 @@ def run_configs(a, dev, world, reps=30):
         for b in range(B):
             kc.prefill_slot(b, k[b:b + 1])
             vc.prefill_slot(b, v[b:b + 1])
-        ns, _ = kernels.plan_splits(B, Hkv, T, dev)
+        ns, _ = kernels.call_plan(B, Hkv, T, dev, a.num_warps)
         nbytes, raw_rows = algorithmic_bytes(kc, vc, B, Hkv, Hq, T, ns)
 
         def per_call(fn):

@@ -57,6 +57,13 @@ struct AttnArgs {
   const int32_t* T_dev;         // if set, sequence b's valid length is T_dev[b * T_stride] + T_add
   int T_add, T_stride;          // (T is then the capacity; T_stride 0: one length for the batch)
   int ns, split_len, s0, nsl, n_items, ngroups;
+  // Balanced partition (bal_G > 0): the bal_W = units x bal_Su stages of the
+  // launch (a unit = one sequence's head group, bal_Su stages of WPH pages
+  // each) are cut into bal_G equal runs, one per CTA (the grid is bal_G); the
+  // j-th piece of CTA c's run inside one unit is item c + j * bal_G, and it is
+  // split number c - (first CTA touching the unit) of that unit.
+  int bal_G, bal_Su;
+  int64_t bal_W;
   float qk_scale;
   // Paged caches: page pg of sequence b is page pages[b * pages_stride + pg] of
   // a pool of pool_pages pages (the cache buffers seen as [pool_pages, 16, H,
@@ -134,6 +141,7 @@ __device__ __forceinline__ Slot tile_ptrs(const uint8_t* stage, int h, int ph) {
 
 struct Item {
   int b, hg, split, tok0, tok1, page0, npages;
+  int fill_to;  // splits split+1 .. fill_to-1 of the unit get empty partials from this item
 };
 
 // Valid tokens of this launch: the host's T, or the device-side length (a
@@ -168,10 +176,35 @@ __device__ __forceinline__ int item_split_len(const AttnArgs& a, int T) {
   return max(1, ((T + kP - 1) / kP + a.ns - 1) / a.ns) * kP;
 }
 
+template <int WPH>
 __device__ __forceinline__ Item decode_item(const AttnArgs& a, int item) {
   Item it;
+  if (a.bal_G > 0) {
+    const int64_t G = a.bal_G, W = a.bal_W, Su = a.bal_Su;
+    const int64_t c = item % G, j = item / G;
+    const int64_t lo = c * W / G, hi = (c + 1) * W / G;
+    const int64_t u = lo / Su + j;
+    const int64_t s0 = max(lo, u * Su), s1 = min(hi, (u + 1) * Su);
+    it.b = static_cast<int>(u / a.ngroups);
+    it.hg = static_cast<int>(u % a.ngroups);
+    if (s0 >= s1 || u * Su >= W) {  // past this CTA's run: no pages, no partial
+      it.split = -1;
+      it.fill_to = -1;
+      it.tok0 = it.tok1 = it.page0 = it.npages = 0;
+      return it;
+    }
+    const int64_t first = ((u * Su + 1) * G + W - 1) / W - 1;  // the CTA whose run holds the unit's first stage
+    it.split = static_cast<int>(c - first);
+    it.fill_to = s1 == (u + 1) * Su ? a.ns : it.split + 1;     // the unit's last piece closes its splits
+    it.tok0 = static_cast<int>((s0 - u * Su) * WPH * kP);
+    it.tok1 = max(it.tok0, min(static_cast<int>((s1 - u * Su) * WPH * kP), a.T));
+    it.page0 = it.tok0 / kP;
+    it.npages = (it.tok1 - it.tok0 + kP - 1) / kP;
+    return it;
+  }
   const int bg = item / a.nsl;
   it.split = a.s0 + item % a.nsl;
+  it.fill_to = it.split + 1;
   it.b = bg / a.ngroups;
   it.hg = bg % a.ngroups;
   const int T = valid_tokens(a, it.b);
@@ -983,7 +1016,7 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
     Item it{};
     // the cursor skips items without pages (splits past the valid length)
     for (; item < a.n_items; item += gridDim.x) {
-      it = decode_item(a, item);
+      it = decode_item<WPH>(a, item);
       nst = (it.npages + WPH - 1) / WPH;
       if (nst > 0) break;
     }
@@ -1058,7 +1091,7 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
       if (++s == nst) {
         s = 0;
         for (item += gridDim.x; item < a.n_items; item += gridDim.x) {
-          it = decode_item(a, item);
+          it = decode_item<WPH>(a, item);
           nst = (it.npages + WPH - 1) / WPH;
           if (nst > 0) break;
         }
@@ -1087,7 +1120,7 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
   uint32_t qf[NT][16];
 
   for (int item = blockIdx.x; item < a.n_items; item += gridDim.x) {
-    const Item it = decode_item(a, item);
+    const Item it = decode_item<WPH>(a, item);
     const int hk = it.hg * HG + hl;
     const int nst = (it.npages + WPH - 1) / WPH;
     load_q<NT>(a, it.b, hk, g, t, qf);
@@ -1156,6 +1189,22 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);
       }
+    }
+
+    if (it.split < 0) continue;  // a balanced plan's empty piece: no partial to write
+    // splits of the unit that no CTA holds (a balanced plan): empty partials
+    // (m = -inf, l = 0, o = 0), which the merge weighs with 0
+    if (it.fill_to > it.split + 1 && ph == 0) {
+      const int64_t r0 = static_cast<int64_t>(it.b) * a.Hq + static_cast<int64_t>(hk) * a.G;
+      for (int h = 0; h < a.G; ++h)
+        for (int sp = it.split + 1; sp < it.fill_to; ++sp) {
+          const int64_t col = (r0 + h) * a.ns + sp;
+          reinterpret_cast<float4*>(a.ws_o + col * kD)[lane] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (lane == 0) {
+            a.ws_m[col] = -INFINITY;
+            a.ws_l[col] = 0.f;
+          }
+        }
     }
 
     // ---- finish the item: full l per head, then (if several page phases) merge them
@@ -1395,10 +1444,12 @@ int common_args(AttnArgs& a, const uint16_t* q, int B, int TS, int Hkv, int Hq, 
   if (Hq % Hkv != 0) return EXK_EARG;
   if (Hq / Hkv > 16) return EXK_EHEADS;
   if (nwc != 4 && nwc != 8) return EXK_EARG;
-  if (ws->ns <= 0 || ws->split_len <= 0 || ws->split_len % kP != 0) return EXK_EARG;
-  if (static_cast<int64_t>(ws->ns) * ws->split_len < T) return EXK_EARG;
+  const bool bal = ws->split_len == 0;  // a balanced plan (exk_plan_balanced): the whole call only
+  if (ws->ns <= 0 || ws->split_len < 0 || ws->split_len % kP != 0) return EXK_EARG;
+  if (bal && (s0 != 0 || s1 != ws->ns)) return EXK_EARG;
+  if (!bal && static_cast<int64_t>(ws->ns) * ws->split_len < T) return EXK_EARG;
   if (s0 < 0 || s1 > ws->ns || s0 >= s1) return EXK_EARG;
-  if (static_cast<int64_t>(s0) * ws->split_len >= T) return EXK_EARG;
+  if (!bal && static_cast<int64_t>(s0) * ws->split_len >= T) return EXK_EARG;
   if (!aligned16(q) || !aligned16(ws->o)) return EXK_EALIGN;
   if (static_cast<int64_t>(B) * TS * Hkv > (int64_t{1} << 31) - 1) return EXK_EARG;
   a.q = q;
@@ -1420,8 +1471,11 @@ int common_args(AttnArgs& a, const uint16_t* q, int B, int TS, int Hkv, int Hq, 
   a.split_len = ws->split_len;
   a.s0 = s0;
   // splits entirely past T (possible when s1 > the plan's last split) hold no work
-  const int last = (T - 1) / ws->split_len;
+  const int last = bal ? s1 - 1 : (T - 1) / ws->split_len;
   a.nsl = std::min(s1, last + 1) - s0;
+  a.bal_G = 0;
+  a.bal_Su = 0;
+  a.bal_W = 0;
   const int hg = item_heads(ws, Hkv, nwc);
   if (hg <= 0) return EXK_EARG;
   a.ngroups = Hkv / hg;
@@ -1502,6 +1556,66 @@ extern "C" int exk_plan_splits(int B, int Hkv, int T, int num_ctas, int32_t* ns_
 
 namespace {
 
+// The balanced partition of a launch: units of Su stages, cut into G equal runs.
+struct Balance {
+  int64_t units, Su, W, G;
+  int splits;    // most pieces one unit is cut into (the workspace columns needed)
+  int pieces;    // most pieces one CTA's run holds (items per CTA)
+};
+
+Balance balance_of(int B, int ngroups, int T, int wph, int ctas) {
+  Balance b;
+  b.units = static_cast<int64_t>(B) * ngroups;
+  const int64_t npt = (T + kP - 1) / kP;
+  b.Su = (npt + wph - 1) / wph;
+  b.W = b.units * b.Su;
+  b.G = std::min<int64_t>(ctas, b.W);
+  auto lo = [&](int64_t c) { return c * b.W / b.G; };
+  auto owner = [&](int64_t x) { return ((x + 1) * b.G + b.W - 1) / b.W - 1; };  // the CTA whose run holds stage x
+  b.splits = 1;
+  for (int64_t u = 0; u < b.units; ++u)
+    b.splits = static_cast<int>(std::max<int64_t>(b.splits, owner((u + 1) * b.Su - 1) - owner(u * b.Su) + 1));
+  b.pieces = 1;
+  for (int64_t c = 0; c < b.G; ++c)
+    b.pieces = static_cast<int>(std::max<int64_t>(b.pieces, (lo(c + 1) - 1) / b.Su - lo(c) / b.Su + 1));
+  return b;
+}
+
+// Fills the balanced partition of a whole-call launch (ws->split_len == 0):
+// host lengths and contiguous caches only; the grid is then exactly bal_G.
+int balance_args(AttnArgs& a, const exk_partials* ws, int hg, int wph, int sms) {
+  if (ws->split_len != 0) return 0;
+  if (a.T_dev != nullptr || a.pages != nullptr) return EXK_EARG;
+  const Balance b = balance_of(a.B, a.Hkv / hg, a.T, wph, sms);
+  if (b.splits > ws->ns) return EXK_EARG;  // the workspace must hold every piece of a unit
+  if (b.G * b.pieces > (int64_t{1} << 30)) return EXK_EARG;
+  a.bal_G = static_cast<int>(b.G);
+  a.bal_Su = static_cast<int>(b.Su);
+  a.bal_W = b.W;
+  a.n_items = static_cast<int>(b.G * b.pieces);
+  return 0;
+}
+
+}  // namespace
+
+extern "C" int exk_plan_balanced(int B, int Hkv, int T, int num_ctas, int consumer_warps, int32_t* ns_out) {
+  if (B <= 0 || Hkv <= 0 || T <= 0 || num_ctas <= 0 || ns_out == nullptr) return EXK_EARG;
+  if (consumer_warps != 4 && consumer_warps != 8) return EXK_EARG;
+  const int hg = std::min(head_group(Hkv), consumer_warps);
+  const int wph = consumer_warps / hg;
+  const Balance b = balance_of(B, Hkv / hg, T, wph, num_ctas);
+  // stages on the busiest CTA, each piece (item) costing ~2 stages of fixed
+  // work (Q load, pipeline refill, epilogue), against the uniform plan's
+  constexpr int64_t kItemOverhead = 2;
+  const int64_t bal_cost = (b.W + b.G - 1) / b.G + kItemOverhead * b.pieces;
+  int32_t ns = 0, sl = 0;
+  const int64_t uni_cost = plan_for_heads(B, Hkv, T, num_ctas, hg, &ns, &sl);
+  *ns_out = (bal_cost < uni_cost && b.splits <= 4096) ? b.splits : 0;
+  return 0;
+}
+
+namespace {
+
 // A paged call (pages != nullptr) reads its pages from a pool of pool_pages
 // pages through the block table; it needs one page per head per stage (the
 // head group equal to the consumer warps), since consecutive pages of a
@@ -1533,6 +1647,7 @@ int split_compressed(const uint16_t* q, const exk_cview* k, const exk_cview* v, 
   int sms = 0;
   if ((r = use_device(device, &sms)) != 0) return r;
   const int wph = consumer_warps / hg;
+  if ((r = balance_args(a, ws, hg, wph, sms)) != 0) return r;
   const exk_cview* cv[2] = {k, v};
   AttnMaps maps;
   const int64_t rows = pages ? static_cast<int64_t>(pool_pages) * kP : static_cast<int64_t>(B) * TS;
@@ -1555,7 +1670,7 @@ int split_compressed(const uint16_t* q, const exk_cview* k, const exk_cview* v, 
                             wph, hg, CU_TENSOR_MAP_SWIZZLE_NONE)) != 0)
       return r;
   }
-  const int grid = static_cast<int>(std::min<int64_t>(a.n_items, sms));
+  const int grid = a.bal_G > 0 ? a.bal_G : static_cast<int>(std::min<int64_t>(a.n_items, sms));
   return dispatch_split<true>(a, maps, hg, grid, consumer_warps, device, static_cast<cudaStream_t>(stream));
 }
 
@@ -1576,6 +1691,7 @@ int split_bf16(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, i
   if ((r = use_device(device, &sms)) != 0) return r;
   if (!aligned16(k) || !aligned16(v)) return EXK_EALIGN;
   const int wph = consumer_warps / hg;
+  if ((r = balance_args(a, ws, hg, wph, sms)) != 0) return r;
   AttnMaps maps;
   const int64_t rows = pages ? static_cast<int64_t>(pool_pages) * kP : static_cast<int64_t>(B) * TS;
   if ((r = head_major_map(&maps.m[0], CU_TENSOR_MAP_DATA_TYPE_UINT16, k, 128, 2, rows, Hkv, 64, kP * wph, hg,
@@ -1584,7 +1700,7 @@ int split_bf16(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, i
   if ((r = head_major_map(&maps.m[1], CU_TENSOR_MAP_DATA_TYPE_UINT16, v, 128, 2, rows, Hkv, 64, kP * wph, hg,
                           CU_TENSOR_MAP_SWIZZLE_128B)) != 0)
     return r;
-  const int grid = static_cast<int>(std::min<int64_t>(a.n_items, sms));
+  const int grid = a.bal_G > 0 ? a.bal_G : static_cast<int>(std::min<int64_t>(a.n_items, sms));
   return dispatch_split<false>(a, maps, hg, grid, consumer_warps, device, static_cast<cudaStream_t>(stream));
 }
 

@@ -9,8 +9,9 @@ check_status(). There is no CPU or Triton fallback: without the library this
 module fails to import.
 
 Differences from the reference, all invisible to callers of the reference API:
-  * the split layout comes from plan_splits() (persistent CTAs over the SMs)
-    instead of choose_split(); choose_split() is kept for compatibility;
+  * the split layout comes from call_plan() (persistent CTAs over the SMs:
+    equal-length splits, or one equal run of pages per CTA when that balances
+    better) instead of choose_split(); choose_split() is kept for compatibility;
   * BLOCK_N and num_stages are accepted and ignored (pages are 16 tokens and
     the TMA ring depth is fixed); num_warps selects 4 or 8 consumer warps
     (default 8) — the compressed and bf16 kernels called with the same value
@@ -62,6 +63,20 @@ def plan_splits(B, Hkv, T, device=None, num_ctas=None):
     ctas = num_ctas if num_ctas is not None else num_sms(device)
     check(lib.exk_plan_splits(B, Hkv, T, ctas, ctypes.byref(ns), ctypes.byref(sl)), "exk_plan_splits")
     return ns.value, sl.value
+
+
+def call_plan(B, Hkv, T, device=None, num_warps=None, num_ctas=None):
+    """(splits, split length) for one whole decode-attention call with host-side T:
+    the balanced plan (split length 0: every CTA gets an equal run of the call's
+    pages across sequence boundaries; exk_plan_balanced) when it is estimated
+    faster than the uniform plan of plan_splits(), else the uniform one. The
+    compressed and bf16 calls with the same arguments get the same plan."""
+    ns = _I32()
+    ctas = num_ctas if num_ctas is not None else num_sms(device)
+    check(lib.exk_plan_balanced(B, Hkv, T, ctas, _consumer_warps(num_warps), ctypes.byref(ns)), "exk_plan_balanced")
+    if ns.value > 0:
+        return ns.value, 0
+    return plan_splits(B, Hkv, T, device, num_ctas)
 
 
 def _device_index(device):
@@ -228,7 +243,7 @@ def attention_compressed(q, kc, vc, T, BLOCK_N=64, num_warps=None, num_stages=1)
     B, Hq, _ = q.shape
     dev = q.device.index
     stream = torch.cuda.current_stream(q.device).cuda_stream
-    ns, sl = plan_splits(B, Hkv, T, dev)
+    ns, sl = call_plan(B, Hkv, T, dev, num_warps)
     ws = _workspace(q.device, stream, B * Hq, ns, sl)
     out = torch.empty_like(q)
     rc = lib.exk_attention_compressed(q.data_ptr(), ctypes.byref(ka), ctypes.byref(va), B, TS, Hkv, Hq, T,
@@ -247,7 +262,7 @@ def attention_reference(q, k, v, T, BLOCK_N=64, num_warps=None, num_stages=1):
     B, Hq, _ = q.shape
     dev = q.device.index
     stream = torch.cuda.current_stream(q.device).cuda_stream
-    ns, sl = plan_splits(B, Hkv, T, dev)
+    ns, sl = call_plan(B, Hkv, T, dev, num_warps)
     ws = _workspace(q.device, stream, B * Hq, ns, sl)
     out = torch.empty_like(q)
     rc = lib.exk_attention_bf16(q.data_ptr(), k.data_ptr(), v.data_ptr(), B, TS, Hkv, Hq, T, ctypes.byref(ws[3]),

@@ -80,7 +80,9 @@ typedef struct exk_cview {
  * (sum of exp2(s - m)); rows = B * Hq. With the plan: ns splits of split_len
  * tokens, and `heads`, the KV heads one work item (one CTA at a time) covers:
  * 1, 2, 4 or 8 dividing Hkv, or 0 for the default (up to 8). The partials of
- * a split depend on `heads`, so calls that must agree bit for bit share it. */
+ * a split depend on `heads`, so calls that must agree bit for bit share it.
+ * split_len = 0 selects a balanced plan (exk_plan_balanced): the whole call
+ * only (splits [0, ns)), host-side T, contiguous caches. */
 typedef struct exk_partials {
   float *o;
   float *m;
@@ -96,6 +98,18 @@ typedef struct exk_partials {
  * (exactkv/kernels.py:273-277); the layout depends only on the arguments, so
  * the compressed and bf16 kernels and every GPU of a KV split share it. */
 int exk_plan_splits(int B, int Hkv, int T, int num_ctas, int32_t *ns, int32_t *split_len);
+
+/* Balanced plan for one whole call (the split kernel over every split, then
+ * the merge) with host-side T: the (sequence, head group) stages of the call
+ * are cut into num_ctas equal contiguous runs, one per CTA, across sequence
+ * boundaries, so no CTA carries more work than another (with equal-length
+ * splits, a batch whose work items do not fill whole waves leaves some CTAs
+ * idle at the end). A unit's pieces are its splits; *ns receives the most
+ * pieces any unit is cut into (use it with split_len = 0 in exk_partials), or
+ * 0 when the uniform plan of exk_plan_splits is estimated faster. Replaces
+ * choose_split() (exactkv/kernels.py:273-277) for whole calls; the bf16 and
+ * compressed kernels given the same plan cut the work identically. */
+int exk_plan_balanced(int B, int Hkv, int T, int num_ctas, int consumer_warps, int32_t *ns);
 
 /* Number of SMs of a device (the default `num_ctas`). */
 int exk_num_sms(int device);

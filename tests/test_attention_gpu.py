@@ -163,7 +163,8 @@ def test_attention_split_subsets_match_full_run():
         assert torch.equal(x, y)
     out = torch.empty_like(q)
     kernels.merge_partials(ws_b, B * Hq, out)
-    assert same_bits(out, ekv.decode_attention(q, kc, vc))
+    assert same_bits(out, kernels.merge_partials(ws_a, B * Hq, torch.empty_like(q)))
+    _check_close(out, q, k, v, T)
     kernels.check_status()
 
 
@@ -230,3 +231,52 @@ def test_attention_1x128k_raw_pool_stress():
     assert same_bits(o_c, o_r)
     assert same_bits(kernels.decode_to_bf16(kc.buffers(), T), k)
     kernels.check_status()
+
+
+@pytest.mark.parametrize("B,T,Hq,Hkv,nw", [(40, 300, 32, 8, 8), (2, 8190, 32, 8, 8), (3, 1000, 28, 4, 8),
+                                           (6, 777, 16, 2, 4), (5, 4096, 32, 8, 8)])
+def test_balanced_plan(B, T, Hq, Hkv, nw):
+    """The balanced plan (exk_partials.split_len = 0): every CTA gets an equal
+    run of the call's stages, across sequence boundaries (many units per CTA at
+    40 x 300; a unit cut into ~70 pieces at 2 x 8190, which takes the wide
+    merge). The workspace has more columns than any unit needs, so the unit's
+    last piece must close the rest with empty partials. Compressed == bf16 bit
+    for bit, within tolerance of float64 and of the oracle, and within
+    tolerance of the uniform plan's output."""
+    TS = -(-T // 16) * 16
+    k = synthetic.make_kv(B, TS, Hkv, seed=91, key=True, raw_frac=0.01)
+    v = synthetic.make_kv(B, TS, Hkv, seed=92, key=False, raw_frac=0.01)
+    q = synthetic.make_q(B, Hq, seed=93)
+    kc, vc = _compress(k), _compress(v)
+    ns = 160
+    ws_c = kernels._workspace(q.device, 11, B * Hq, ns, 0)
+    ws_r = kernels._workspace(q.device, 12, B * Hq, ns, 0)
+    for ws in (ws_c, ws_r):                      # stale values in every column: all must be rewritten
+        ws[0].fill_(float("nan"))
+        ws[1].fill_(float("nan"))
+        ws[2].fill_(float("nan"))
+    kernels.attention_split(q, kc, vc, T, ws_c, 0, ns, num_warps=nw)
+    kernels.attention_split_bf16(q, k, v, T, ws_r, 0, ns, num_warps=nw)
+    o_c = kernels.merge_partials(ws_c, B * Hq, torch.empty_like(q))
+    o_r = kernels.merge_partials(ws_r, B * Hq, torch.empty_like(q))
+    assert same_bits(o_c, o_r)
+    assert not torch.isnan(o_c.float()).any()
+    _check_close(o_c, q, k, v, T)
+    ns_u, sl_u = kernels.plan_splits(B, Hkv, T)
+    ws_u = kernels._workspace(q.device, 13, B * Hq, ns_u, sl_u)
+    kernels.attention_split(q, kc, vc, T, ws_u, 0, ns_u, num_warps=nw)
+    o_u = kernels.merge_partials(ws_u, B * Hq, torch.empty_like(q))
+    qb, kb, vb = to_bits(q), to_bits(k), to_bits(v)
+    want = bits_to_f32(to_bits(o_u)).astype(np.float64)
+    got = bits_to_f32(to_bits(o_c)).astype(np.float64)
+    assert (np.abs(got - want) <= oatt.tolerance(qb, kb, vb, T, want)).all()
+    kernels.check_status()
+
+
+def test_whole_call_uses_the_balanced_plan_where_it_balances():
+    """At the headline shape (32 x 4096, 8 KV heads, 148 SMs) equal splits leave
+    the busiest CTAs 58 pages against an average of 55.35: the whole-call plan
+    is the balanced one there, and the uniform one where items fill the waves."""
+    assert kernels.call_plan(32, 8, 4096, num_ctas=148)[1] == 0
+    assert kernels.call_plan(8, 8, 8192, num_ctas=148)[1] > 0
+    assert kernels.call_plan(1, 4, 32768, num_ctas=148)[1] > 0

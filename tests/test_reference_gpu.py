@@ -200,7 +200,7 @@ def test_absolute_error_against_the_reference(case):
     ref32 = _merged64(*wr)
     ok, ov = _our_cache(k, T), _our_cache(v, T)
     o_ours = kernels.attention_compressed(q, ok, ov, T)
-    ns_o, _ = kernels.plan_splits(B, Hkv, T)
+    ns_o, _ = kernels.call_plan(B, Hkv, T)
     wo = kernels._WS[(q.device.index, stream, B * Hq, ns_o)]
     ours32 = _merged64(*wo[:3])
     assert torch.equal(o_ours.view(torch.int16), kernels.attention_reference(q, k, v, T).view(torch.int16))

@@ -3,8 +3,8 @@ cannot allocate device memory when they call (a runtime that plans all device
 memory up front, a plugin whose enqueue must not call cudaMalloc). It keeps its
 split partials in a fixed array inside the library instead of a workspace.
 
-Checked through the C ABI against the allocating entry point (attention_compressed:
-exk_attn_split_compressed + exk_attn_merge with a torch workspace) on two calls in
+Checked through the C ABI against the allocating entry points
+(exk_attn_split_compressed + exk_attn_merge with a torch workspace) on two calls in
 a row — the second reuses the array the first left behind — within the tolerance
 the attention tests use (oracle.attention.tolerance), and bit for bit, since both
 run the same kernels on the same split plan. Also: a request whose partials do not
@@ -60,7 +60,12 @@ def test_noalloc_matches_allocating_entry_point(B, T, Hq, Hkv):
     for q in qs:                                               # two calls in a row
         out = torch.empty_like(q)
         assert _call_noalloc(q, kc, vc, T, out) == 0
-        ref = kernels.attention_compressed(q, kc, vc, T)
+        # the allocating entry points on the same (uniform) plan: exk_attn_split_compressed
+        # over every split into a torch workspace, then exk_attn_merge
+        ns, sl = kernels.plan_splits(B, Hkv, T)
+        ws = kernels._workspace(q.device, 3, B * Hq, ns, sl)       # a private workspace key
+        kernels.attention_split(q, kc, vc, T, ws, 0, ns)
+        ref = kernels.merge_partials(ws, B * Hq, torch.empty_like(q))
         got = bits_to_f32(to_bits(out)).astype(np.float64)
         want = bits_to_f32(to_bits(ref)).astype(np.float64)
         tol = oatt.tolerance(to_bits(q), kb, vb, T, want)
