@@ -110,6 +110,8 @@ def parse_args():
     ap.add_argument("--engine-real-prompts", type=int, default=16,
                     help="sequences per engine prefilled from random-id prompts through the model")
     ap.add_argument("--num-warps", type=int, default=8)
+    ap.add_argument("--only-config", choices=("qwen2.5-7b_1x32768", "llama3.1-8b_8x8192"),
+                    help="run only that config's calls (a short command to profile) and exit")
     ap.add_argument("--record-traffic", metavar="NCU_REP",
                     help="write the split kernel's per-launch DRAM bytes from an ncu report and exit")
     ap.add_argument("--traffic-batch", type=int, default=16, help="batch of the --record-traffic capture")
@@ -711,6 +713,40 @@ def run_e2e(a, kc, vc, B, Hq, Hkv, T0, dev, world, raw_rows0, ns0):
                     "into pinned host memory over PCIe (the D2H bytes); context grows from 4096"}
 
 
+CONFIGS = {"qwen2.5-7b_1x32768": (1, 32768, 28, 4, 1e6), "llama3.1-8b_8x8192": (8, 8192, 32, 8, 5e5)}
+
+
+def run_one_config(a, dev):
+    """--only-config NAME: that config's compressed call (split + merge) a.steps
+    times after a.warmup, nothing else (a short command for ncu captures)."""
+    import torch
+
+    import exactkv_b200 as ekv
+    from exactkv_b200 import kernels, synthetic
+    B, T, Hq, Hkv, theta = CONFIGS[a.only_config]
+    k = synthetic.make_kv(B, T, Hkv, seed=700, theta=theta, key=True, device=dev)
+    v = synthetic.make_kv(B, T, Hkv, seed=701, theta=theta, key=False, device=dev)
+    q = synthetic.make_q(B, Hq, seed=702, device=dev)
+    kc, vc = ekv.CompressedKV(B, T, Hkv, 128, device=dev), ekv.CompressedKV(B, T, Hkv, 128, device=dev)
+    for b in range(B):
+        kc.prefill_slot(b, k[b:b + 1])
+        vc.prefill_slot(b, v[b:b + 1])
+    del k, v
+    for _ in range(a.warmup):
+        ekv.decode_attention(q, kc, vc, num_warps=a.num_warps)
+    stream = torch.cuda.current_stream(dev)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(a.steps):
+        ekv.decode_attention(q, kc, vc, num_warps=a.num_warps)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    kernels.check_status(dev)
+    print(json.dumps({"config": a.only_config, "us_per_call": round(e0.elapsed_time(e1) * 1e3 / a.steps, 2),
+                      "note": "back-to-back calls (cache in L2 when it fits); for profiling"}))
+
+
 def run_configs(a, dev, world, reps=30):
     """BASELINE configs[1] (Qwen2.5-7B 1 x 32768, 28 q / 4 kv, RoPE theta 1e6) and
     the second shape of configs[2] (Llama 8 x 8192, 32 q / 8 kv): one
@@ -727,8 +763,7 @@ def run_configs(a, dev, world, reps=30):
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
     out = {}
-    for name, (B, T, Hq, Hkv, theta) in {"qwen2.5-7b_1x32768": (1, 32768, 28, 4, 1e6),
-                                         "llama3.1-8b_8x8192": (8, 8192, 32, 8, 5e5)}.items():
+    for name, (B, T, Hq, Hkv, theta) in CONFIGS.items():
         k = synthetic.make_kv(B, T, Hkv, seed=700, theta=theta, key=True, device=dev)
         v = synthetic.make_kv(B, T, Hkv, seed=701, theta=theta, key=False, device=dev)
         q = synthetic.make_q(B, Hq, seed=702, device=dev)
@@ -1187,6 +1222,11 @@ def main():
         record_traffic(a.record_traffic, a.traffic_batch, 32 / a.traffic_batch)
         return 0
     rank, world, local = dist_env()
+    if a.only_config:
+        import torch
+        torch.cuda.set_device(local)
+        run_one_config(a, torch.device("cuda", local))
+        return 0
     if a.impl == "reference":
         run_reference(a, rank, world)
         return 0
