@@ -84,7 +84,7 @@ class CompressedKV:
         self.cnt = torch.zeros(1, **i32)                 # pool slots taken by encoded pages
         self.pool = RawPool(B, H, D, max(64, int(B * TS * H * reserve)), self.dev)
         self.lens = [0] * B                              # tokens per sequence
-        self.T = 0                                       # tokens of the batch (the longest sequence)
+        self.T = 0                                       # tokens of the batch (the last prefilled slot's, as the reference)
         self._t_dev = torch.zeros(1, **i32)              # T on the device, for the append kernel
         self._t_dev_stale = False                        # T moved by device-length steps
         self._checked = True                             # headroom verified since the last page boundary
