@@ -668,7 +668,7 @@ def run_e2e(a, kc, vc, B, Hq, Hkv, T0, dev, world, raw_rows0, ns0):
         kernels.attention_compressed_devlen(q_in, kc, vc, length.t, 1, out=out, advance=1)
 
     gs = GraphedStep(body, length, check_pages=8)
-    ns_cap, _ = kernels.plan_splits(B, Hkv, kc.TS, dev)
+    ns_cap, _ = kernels.devlen_plan(B, Hkv, kc.TS, length.t, dev)
 
     def one(i):
         inp.copy_(inp_h[i], non_blocking=True)

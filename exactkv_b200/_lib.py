@@ -32,7 +32,7 @@ class Partials(ctypes.Structure):
 _P = ctypes.POINTER
 _SIGNATURES.update({
     "exk_plan_splits": (c_int, [c_int, c_int, c_int, c_int, _P(c_int32), _P(c_int32)]),
-    "exk_plan_balanced": (c_int, [c_int, c_int, c_int, c_int, c_int, _P(c_int32)]),
+    "exk_plan_balanced": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, _P(c_int32)]),
     "exk_num_sms": (c_int, [c_int]),
     "exk_attn_split_compressed": (c_int, [c_void_p, _P(CView), _P(CView), c_int, c_int, c_int, c_int, c_int,
                                           c_int, c_int, _P(Partials), c_int, c_float, c_void_p, c_int, c_void_p]),

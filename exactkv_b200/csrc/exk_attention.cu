@@ -180,7 +180,16 @@ template <int WPH>
 __device__ __forceinline__ Item decode_item(const AttnArgs& a, int item) {
   Item it;
   if (a.bal_G > 0) {
-    const int64_t G = a.bal_G, W = a.bal_W, Su = a.bal_Su;
+    const int64_t G = a.bal_G;
+    int64_t W = a.bal_W, Su = a.bal_Su;
+    int T = a.T;
+    if (a.T_dev != nullptr) {
+      // one device-side length for the batch: the partition follows it (a
+      // length of 0 keeps one empty stage per unit, so every split is closed)
+      T = valid_tokens(a, 0);
+      Su = max(1, ((T + kP - 1) / kP + WPH - 1) / WPH);
+      W = static_cast<int64_t>(a.B) * a.ngroups * Su;
+    }
     const int64_t c = item % G, j = item / G;
     const int64_t lo = c * W / G, hi = (c + 1) * W / G;
     const int64_t u = lo / Su + j;
@@ -188,16 +197,21 @@ __device__ __forceinline__ Item decode_item(const AttnArgs& a, int item) {
     it.b = static_cast<int>(u / a.ngroups);
     it.hg = static_cast<int>(u % a.ngroups);
     if (s0 >= s1 || u * Su >= W) {  // past this CTA's run: no pages, no partial
+      it.b = it.hg = 0;              // (u may lie past the last unit)
       it.split = -1;
       it.fill_to = -1;
       it.tok0 = it.tok1 = it.page0 = it.npages = 0;
       return it;
     }
-    const int64_t first = ((u * Su + 1) * G + W - 1) / W - 1;  // the CTA whose run holds the unit's first stage
+    // the CTA whose run holds stage x (runs are empty where there are fewer stages than CTAs)
+    auto owner = [&](int64_t x) { return ((x + 1) * G + W - 1) / W - 1; };
+    const int64_t first = owner(u * Su);
     it.split = static_cast<int>(c - first);
-    it.fill_to = s1 == (u + 1) * Su ? a.ns : it.split + 1;     // the unit's last piece closes its splits
+    // the piece closes the columns of the empty runs up to the unit's next
+    // piece, and the unit's last piece every column after it
+    it.fill_to = s1 == (u + 1) * Su ? a.ns : static_cast<int>(owner(s1) - first);
     it.tok0 = static_cast<int>((s0 - u * Su) * WPH * kP);
-    it.tok1 = max(it.tok0, min(static_cast<int>((s1 - u * Su) * WPH * kP), a.T));
+    it.tok1 = max(it.tok0, min(static_cast<int>((s1 - u * Su) * WPH * kP), T));
     it.page0 = it.tok0 / kP;
     it.npages = (it.tok1 - it.tok0 + kP - 1) / kP;
     return it;
@@ -1121,6 +1135,7 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
 
   for (int item = blockIdx.x; item < a.n_items; item += gridDim.x) {
     const Item it = decode_item<WPH>(a, item);
+    if (it.split < 0) continue;  // a balanced plan's empty piece: no pages, no partial
     const int hk = it.hg * HG + hl;
     const int nst = (it.npages + WPH - 1) / WPH;
     load_q<NT>(a, it.b, hk, g, t, qf);
@@ -1191,7 +1206,6 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1)
       }
     }
 
-    if (it.split < 0) continue;  // a balanced plan's empty piece: no partial to write
     // splits of the unit that no CTA holds (a balanced plan): empty partials
     // (m = -inf, l = 0, o = 0), which the merge weighs with 0
     if (it.fill_to > it.split + 1 && ph == 0) {
@@ -1569,7 +1583,9 @@ Balance balance_of(int B, int ngroups, int T, int wph, int ctas) {
   const int64_t npt = (T + kP - 1) / kP;
   b.Su = (npt + wph - 1) / wph;
   b.W = b.units * b.Su;
-  b.G = std::min<int64_t>(ctas, b.W);
+  // every CTA, also with fewer stages than CTAs (runs of 0 or 1 stage), as in a
+  // device-length call, which cuts a length the host does not know
+  b.G = ctas;
   auto lo = [&](int64_t c) { return c * b.W / b.G; };
   auto owner = [&](int64_t x) { return ((x + 1) * b.G + b.W - 1) / b.W - 1; };  // the CTA whose run holds stage x
   b.splits = 1;
@@ -1585,7 +1601,22 @@ Balance balance_of(int B, int ngroups, int T, int wph, int ctas) {
 // host lengths and contiguous caches only; the grid is then exactly bal_G.
 int balance_args(AttnArgs& a, const exk_partials* ws, int hg, int wph, int sms) {
   if (ws->split_len != 0) return 0;
-  if (a.T_dev != nullptr || a.pages != nullptr) return EXK_EARG;
+  if (a.pages != nullptr || (a.T_dev != nullptr && a.T_stride != 0)) return EXK_EARG;
+  if (a.T_dev != nullptr) {
+    // the length is read on the device: bounds that hold for every length up
+    // to the capacity a.T (a unit of Su stages spans at most ceil(G / units) + 1
+    // runs, a run of W / G stages touches at most ceil(units / G) + 1 units)
+    const int64_t units = static_cast<int64_t>(a.B) * (a.Hkv / hg);
+    const int64_t G = sms;
+    const int64_t splits = (G + units - 1) / units + 1, pieces = (units + G - 1) / G + 1;
+    if (splits > ws->ns) return EXK_EARG;
+    if (G * pieces > (int64_t{1} << 30)) return EXK_EARG;
+    a.bal_G = static_cast<int>(G);
+    a.bal_Su = 0;
+    a.bal_W = 0;
+    a.n_items = static_cast<int>(G * pieces);
+    return 0;
+  }
   const Balance b = balance_of(a.B, a.Hkv / hg, a.T, wph, sms);
   if (b.splits > ws->ns) return EXK_EARG;  // the workspace must hold every piece of a unit
   if (b.G * b.pieces > (int64_t{1} << 30)) return EXK_EARG;
@@ -1598,7 +1629,8 @@ int balance_args(AttnArgs& a, const exk_partials* ws, int hg, int wph, int sms) 
 
 }  // namespace
 
-extern "C" int exk_plan_balanced(int B, int Hkv, int T, int num_ctas, int consumer_warps, int32_t* ns_out) {
+extern "C" int exk_plan_balanced(int B, int Hkv, int T, int num_ctas, int consumer_warps, int any_length,
+                                 int32_t* ns_out) {
   if (B <= 0 || Hkv <= 0 || T <= 0 || num_ctas <= 0 || ns_out == nullptr) return EXK_EARG;
   if (consumer_warps != 4 && consumer_warps != 8) return EXK_EARG;
   const int hg = std::min(head_group(Hkv), consumer_warps);
@@ -1610,7 +1642,10 @@ extern "C" int exk_plan_balanced(int B, int Hkv, int T, int num_ctas, int consum
   const int64_t bal_cost = (b.W + b.G - 1) / b.G + kItemOverhead * b.pieces;
   int32_t ns = 0, sl = 0;
   const int64_t uni_cost = plan_for_heads(B, Hkv, T, num_ctas, hg, &ns, &sl);
-  *ns_out = (bal_cost < uni_cost && b.splits <= 4096) ? b.splits : 0;
+  // any_length: the call reads one batch-wide length on the device (at most T):
+  // the workspace bound that holds for every length
+  const int64_t splits = any_length ? (b.G + b.units - 1) / b.units + 1 : b.splits;
+  *ns_out = (bal_cost < uni_cost && splits <= 4096) ? static_cast<int32_t>(splits) : 0;
   return 0;
 }
 
@@ -1761,7 +1796,7 @@ int devlen_args(const exk_partials* ws, const uint16_t* out, const int32_t* T_de
   if ((reinterpret_cast<uintptr_t>(out) & 7u) != 0 || (reinterpret_cast<uintptr_t>(T_dev) & 3u) != 0) return EXK_EALIGN;
   if (device_reachable(out) != 0) return EXK_EARG;
   const int last = (T_cap - 1) / (ws->split_len > 0 ? ws->split_len : 1);
-  if (T_cap <= 0 || last + 1 != ws->ns) return EXK_EARG;  // the plan must be the capacity's
+  if (T_cap <= 0 || (ws->split_len != 0 && last + 1 != ws->ns)) return EXK_EARG;  // the plan must be the capacity's
   return 0;
 }
 

@@ -65,15 +65,18 @@ def plan_splits(B, Hkv, T, device=None, num_ctas=None):
     return ns.value, sl.value
 
 
-def call_plan(B, Hkv, T, device=None, num_warps=None, num_ctas=None):
+def call_plan(B, Hkv, T, device=None, num_warps=None, num_ctas=None, any_length=False):
     """(splits, split length) for one whole decode-attention call with host-side T:
     the balanced plan (split length 0: every CTA gets an equal run of the call's
     pages across sequence boundaries; exk_plan_balanced) when it is estimated
     faster than the uniform plan of plan_splits(), else the uniform one. The
-    compressed and bf16 calls with the same arguments get the same plan."""
+    compressed and bf16 calls with the same arguments get the same plan.
+    any_length: the plan of a device-length call with one length for the batch
+    and capacity T (the balanced plan's kernel cuts the length it reads)."""
     ns = _I32()
     ctas = num_ctas if num_ctas is not None else num_sms(device)
-    check(lib.exk_plan_balanced(B, Hkv, T, ctas, _consumer_warps(num_warps), ctypes.byref(ns)), "exk_plan_balanced")
+    check(lib.exk_plan_balanced(B, Hkv, T, ctas, _consumer_warps(num_warps), int(bool(any_length)),
+                                ctypes.byref(ns)), "exk_plan_balanced")
     if ns.value > 0:
         return ns.value, 0
     return plan_splits(B, Hkv, T, device, num_ctas)
@@ -317,6 +320,15 @@ def _stride_of(T_dev, B):
     return 0 if T_dev.numel() == 1 else 1
 
 
+def devlen_plan(B, Hkv, TS, T_dev, device=None, num_warps=None):
+    """(splits, split length) of a device-length call over caches of capacity
+    TS: with one length for the batch the balanced plan where it is estimated
+    faster (call_plan(any_length=True)), else plan_splits() for the capacity."""
+    if _stride_of(T_dev, B) == 0:
+        return call_plan(B, Hkv, TS, device, num_warps, any_length=True)
+    return plan_splits(B, Hkv, TS, device)
+
+
 def append_token(x, c, T_dev):
     """x [B, H, 128] bf16 (channels contiguous): the step's token for every
     sequence of CompressedKV `c`, appended at row T_dev (one length for the
@@ -350,7 +362,7 @@ def attention_compressed_devlen(q, kc, vc, T_dev, T_add=1, out=None, num_warps=N
     B, Hq, _ = q.shape
     dev = q.device.index
     stream = torch.cuda.current_stream(q.device).cuda_stream
-    ns, sl = plan_splits(B, Hkv, TS, dev)
+    ns, sl = devlen_plan(B, Hkv, TS, T_dev, dev, num_warps)
     ws = _workspace(q.device, stream, B * Hq, ns, sl)
     out = torch.empty_like(q) if out is None else _check_out(out, q)
     rc = lib.exk_attention_compressed_devlen(q.data_ptr(), ctypes.byref(ka), ctypes.byref(va), B, TS, Hkv, Hq, TS,
@@ -442,7 +454,7 @@ def attention_reference_devlen(q, k, v, T_dev, T_add=0, out=None, num_warps=None
     B, Hq, _ = q.shape
     dev = q.device.index
     stream = torch.cuda.current_stream(q.device).cuda_stream
-    ns, sl = plan_splits(B, Hkv, TS, dev)
+    ns, sl = devlen_plan(B, Hkv, TS, T_dev, dev, num_warps)
     ws = _workspace(q.device, stream, B * Hq, ns, sl)
     out = torch.empty_like(q) if out is None else _check_out(out, q)
     rc = lib.exk_attention_bf16_devlen(q.data_ptr(), k.data_ptr(), v.data_ptr(), B, TS, Hkv, Hq, TS, T_dev.data_ptr(),

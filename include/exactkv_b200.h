@@ -82,7 +82,8 @@ typedef struct exk_cview {
  * 1, 2, 4 or 8 dividing Hkv, or 0 for the default (up to 8). The partials of
  * a split depend on `heads`, so calls that must agree bit for bit share it.
  * split_len = 0 selects a balanced plan (exk_plan_balanced): the whole call
- * only (splits [0, ns)), host-side T, contiguous caches. */
+ * only (splits [0, ns)), contiguous caches, host-side T or one device-side
+ * length for the batch. */
 typedef struct exk_partials {
   float *o;
   float *m;
@@ -108,8 +109,14 @@ int exk_plan_splits(int B, int Hkv, int T, int num_ctas, int32_t *ns, int32_t *s
  * pieces any unit is cut into (use it with split_len = 0 in exk_partials), or
  * 0 when the uniform plan of exk_plan_splits is estimated faster. Replaces
  * choose_split() (exactkv/kernels.py:273-277) for whole calls; the bf16 and
- * compressed kernels given the same plan cut the work identically. */
-int exk_plan_balanced(int B, int Hkv, int T, int num_ctas, int consumer_warps, int32_t *ns);
+ * compressed kernels given the same plan cut the work identically.
+ * any_length != 0: the plan of a device-length call with one length for the
+ * batch (exk_attention_*_devlen, T_stride 0) and capacity T; the kernel then
+ * cuts the stages of the length it reads, and *ns is the bound
+ * ceil(num_ctas / units) + 1 (units = B * head groups) that holds for every
+ * length up to T. */
+int exk_plan_balanced(int B, int Hkv, int T, int num_ctas, int consumer_warps, int any_length,
+                      int32_t *ns);
 
 /* Number of SMs of a device (the default `num_ctas`). */
 int exk_num_sms(int device);
@@ -195,7 +202,10 @@ int exk_attention_compressed(const uint16_t *q, const exk_cview *k, const exk_cv
  * sequence b into ns runs of ceil(ceil(T_b / 16) / ns) pages, so the work
  * stays balanced at any length (runs past T_b are empty and weigh nothing).
  * Same results as exk_attention_compressed with ns splits of that length at
- * length T_b (ns <= 256). With advance != 0
+ * length T_b (ns <= 256). With a balanced plan (split_len 0, from
+ * exk_plan_balanced with any_length set; T_stride 0 only) the kernel cuts the
+ * call's stages at the length it reads into one equal run per SM, as
+ * exk_attention_compressed does for a host-side T. With advance != 0
  * (T_stride 0 only) the merge then adds `advance` to *T_dev (the end of a
  * step). No counterpart in the reference (its calls take one host-side T). */
 int exk_attention_compressed_devlen(const uint16_t *q, const exk_cview *k, const exk_cview *v,

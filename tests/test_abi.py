@@ -151,11 +151,15 @@ def test_noalloc_rejects_bad_arguments_before_any_launch():
 def test_balanced_plan_host_side():
     """exk_plan_balanced: the balanced plan's split count where it beats equal
     splits (32 x 4096 on 148 CTAs), 0 where the uniform plan is as good, and
-    argument errors."""
+    argument errors. For a device-length call (any_length) the split count is
+    the bound for every length: ceil(148 / 32 units) + 1."""
     from exactkv_b200._lib import lib
     ns = ctypes.c_int32()
-    assert lib.exk_plan_balanced(32, 8, 4096, 148, 8, ctypes.byref(ns)) == 0 and 2 <= ns.value <= 16
-    assert lib.exk_plan_balanced(8, 8, 8192, 148, 8, ctypes.byref(ns)) == 0 and ns.value == 0
-    assert lib.exk_plan_balanced(1, 4, 32768, 148, 8, ctypes.byref(ns)) == 0 and ns.value == 0
-    assert lib.exk_plan_balanced(0, 8, 4096, 148, 8, ctypes.byref(ns)) == -1
-    assert lib.exk_plan_balanced(32, 8, 4096, 148, 6, ctypes.byref(ns)) == -1
+    assert lib.exk_plan_balanced(32, 8, 4096, 148, 8, 0, ctypes.byref(ns)) == 0 and 2 <= ns.value <= 16
+    assert lib.exk_plan_balanced(32, 8, 4096, 148, 8, 1, ctypes.byref(ns)) == 0 and ns.value == 6
+    assert lib.exk_plan_balanced(40, 8, 1024, 148, 8, 1, ctypes.byref(ns)) == 0 and ns.value == 5
+    assert lib.exk_plan_balanced(8, 8, 8192, 148, 8, 0, ctypes.byref(ns)) == 0 and ns.value == 0
+    assert lib.exk_plan_balanced(1, 4, 32768, 148, 8, 0, ctypes.byref(ns)) == 0 and ns.value == 0
+    assert lib.exk_plan_balanced(1, 4, 32768, 148, 8, 1, ctypes.byref(ns)) == 0 and ns.value == 0
+    assert lib.exk_plan_balanced(0, 8, 4096, 148, 8, 0, ctypes.byref(ns)) == -1
+    assert lib.exk_plan_balanced(32, 8, 4096, 148, 6, 0, ctypes.byref(ns)) == -1

@@ -280,3 +280,71 @@ def test_whole_call_uses_the_balanced_plan_where_it_balances():
     assert kernels.call_plan(32, 8, 4096, num_ctas=148)[1] == 0
     assert kernels.call_plan(8, 8, 8192, num_ctas=148)[1] > 0
     assert kernels.call_plan(1, 4, 32768, num_ctas=148)[1] > 0
+
+
+def _devlen_call(q, kc, vc, T_dev, ws, nw, bf16=False):
+    """exk_attention_{compressed,bf16}_devlen (one length for the batch, T_add 0)
+    over the given workspace: the kernels' own entry points with a chosen plan."""
+    import ctypes
+    from exactkv_b200._lib import lib
+    B, Hq, _ = q.shape
+    dev = q.device.index
+    stream = torch.cuda.current_stream(q.device).cuda_stream
+    out = torch.empty_like(q)
+    common = (T_dev.data_ptr(), 0, 0, 0, ctypes.byref(ws[3]), out.data_ptr(), nw, 128 ** -0.5 * kernels.LOG2E,
+              kernels.status_tensor(dev).data_ptr(), dev, stream)
+    if bf16:
+        TS, Hkv = kc.shape[1], kc.shape[2]
+        rc = lib.exk_attention_bf16_devlen(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), B, TS, Hkv, Hq, TS, *common)
+    else:
+        ka, TS, Hkv = kernels._cache_args(kc)
+        va, _, _ = kernels._cache_args(vc)
+        rc = lib.exk_attention_compressed_devlen(q.data_ptr(), ctypes.byref(ka), ctypes.byref(va), B, TS, Hkv, Hq,
+                                                 TS, *common)
+    kernels.check(rc, "devlen")
+    return out
+
+
+@pytest.mark.parametrize("B,TS,Hq,Hkv,nw", [(32, 4096, 32, 8, 8), (3, 1008, 16, 2, 8), (5, 2048, 28, 4, 4)])
+def test_devlen_balanced_plan_follows_the_device_length(B, TS, Hq, Hkv, nw):
+    """A device-length call with one length for the batch over a balanced plan
+    (split_len 0): the kernel cuts the stages of the length it reads into one
+    equal run per SM, with ceil(SMs / units) + 1 workspace columns (the bound
+    for every length; 51 at 3 x 1008 with 4 page phases per head, which takes
+    the wide merge). At each length (fewer stages than SMs, ragged, the
+    capacity) the output equals, bit for bit, the host-length call with the
+    balanced plan at that length over the same columns, and the bf16 sibling's;
+    at length 0 every column is closed with an empty partial. At the headline
+    shape this is the plan the public device-length call picks."""
+    sms = kernels.num_sms(0)
+    hg = min(max(h for h in (1, 2, 4, 8) if Hkv % h == 0), nw)
+    units = B * (Hkv // hg)
+    ns = -(-sms // units) + 1
+    if (B, TS) == (32, 4096):
+        assert kernels.devlen_plan(B, Hkv, TS, torch.zeros(1, dtype=torch.int32, device="cuda"), num_warps=nw) == (ns, 0)
+    k = synthetic.make_kv(B, TS, Hkv, seed=95, key=True, raw_frac=0.01)
+    v = synthetic.make_kv(B, TS, Hkv, seed=96, key=False, raw_frac=0.01)
+    q = synthetic.make_q(B, Hq, seed=97)
+    kc, vc = _compress(k), _compress(v)
+    ws_d = kernels._workspace(q.device, 21, B * Hq, ns, 0)
+    ws_h = kernels._workspace(q.device, 22, B * Hq, ns, 0)
+    ws_r = kernels._workspace(q.device, 23, B * Hq, ns, 0)
+    T_dev = torch.zeros(1, dtype=torch.int32, device="cuda")
+    for ws in (ws_d, ws_h, ws_r):
+        for t in ws[:3]:
+            t.fill_(float("nan"))
+    _devlen_call(q, kc, vc, T_dev, ws_d, nw)
+    torch.cuda.synchronize()
+    assert torch.all(ws_d[1] == float("-inf")) and torch.all(ws_d[2] == 0) and torch.all(ws_d[0] == 0)
+    for T in (1, 16, 100, TS // 2 + 37, TS - 1, TS):
+        T_dev.fill_(T)
+        o_d = _devlen_call(q, kc, vc, T_dev, ws_d, nw)
+        o_r = _devlen_call(q, k, v, T_dev, ws_r, nw, bf16=True)
+        kernels.attention_split(q, kc, vc, T, ws_h, 0, ns, num_warps=nw)
+        o_h = kernels.merge_partials(ws_h, B * Hq, torch.empty_like(q))
+        assert same_bits(o_d, o_h), T
+        assert same_bits(o_d, o_r), T
+        assert not torch.isnan(o_d.float()).any(), T
+        if T == 100:
+            _check_close(o_d, q, k, v, T)
+    kernels.check_status()
