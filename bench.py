@@ -26,7 +26,10 @@ reasons are sampled through NVML every 5 ms during warm-up and timing.
 
 e2e: the same metric through the public API with host buffers: each step
 copies q [B, Hq, 128] and the new token's K and V [B, Hkv, 128] from pinned
-host memory into the step's device buffers, replays a captured CUDA graph of
+host memory into the step's device buffers (kernels.copy_from_host: the SMs
+read the pinned memory over PCIe; a copy-engine transfer of the same 384 KB
+took 18.5 us plus ~19 us of hand-off to and from the kernels around it),
+replays a captured CUDA graph of
 the device-length decode step (exactkv_b200.graph: append, page encode at
 page boundaries, decode attention, length advance; the raw pools are kept
 ahead with one host sync per 8 pages instead of a sync per page), whose merge
@@ -571,6 +574,12 @@ def time_paged(q, kc, vc, B, T, dev, reps):
                     "vs the contiguous device-length call; back-to-back calls, cache > L2"}
 
 
+# GPU cycles (~0.5 ms) of a spin kernel enqueued before a single timed call, so
+# that the host has enqueued the whole call before its start event runs: the
+# events then time the device work and not the host's launch overhead.
+HOST_AHEAD_CYCLES = 1_000_000
+
+
 def reference_encode_us(src, st, B, T, Hkv, dev, reps):
     """The reference's own encode_pages (Triton) over the same source, when the
     reference package is installed in baseline/_ref (see reference_triton_decode);
@@ -588,6 +597,7 @@ def reference_encode_us(src, st, B, T, Hkv, dev, reps):
         for i in range(reps + 2):
             c.cnt.zero_()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda._sleep(HOST_AHEAD_CYCLES)
             e0.record()
             ref.encode_pages(src, st, c._buf(), 0, 0, B, T // 16)
             e1.record()
@@ -613,6 +623,7 @@ def time_encoder(kbf, B, T, Hkv, dev, reps=5):
     for i in range(reps + 2):
         c.cnt.zero_()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda._sleep(HOST_AHEAD_CYCLES)
         e0.record()
         kernels.encode_pages(src, st, c.encoder_buffers(), 0, 0, B, T // 16)
         e1.record()
@@ -627,7 +638,9 @@ def time_encoder(kbf, B, T, Hkv, dev, reps=5):
     return {"us": round(us, 2), "bf16_read_gbs": round(rows * 256 / us / 1e3, 1),
             "compressed_written_gbs": round(written / us / 1e3, 1), "raw_rows": n,
             "reference_triton_encode_pages_us": ref_us,
-            "what": f"encode_pages over {B} x {T} tokens x {Hkv} heads of keys (4 launches: encode, chunk sums, chunk scan, slot placement + raw copy)"}
+            "what": f"encode_pages over {B} x {T} tokens x {Hkv} heads of keys (4 launches: encode, chunk sums, "
+                    "chunk scan, slot placement + raw copy; each call enqueued behind a spin kernel so the events "
+                    "time the device work, the reference's call likewise)"}
 
 
 def run_e2e(a, kc, vc, B, Hq, Hkv, T0, dev, world, raw_rows0, ns0):
@@ -671,7 +684,7 @@ def run_e2e(a, kc, vc, B, Hq, Hkv, T0, dev, world, raw_rows0, ns0):
     ns_cap, _ = kernels.devlen_plan(B, Hkv, kc.TS, length.t, dev)
 
     def one(i):
-        inp.copy_(inp_h[i], non_blocking=True)
+        kernels.copy_from_host(inp, inp_h[i])     # the SMs read the step's inputs over PCIe
         gs.step()                                 # ends with the output written to host memory
 
     for i in range(2):                            # untimed: the first step captures the graph
@@ -707,7 +720,8 @@ def run_e2e(a, kc, vc, B, Hq, Hkv, T0, dev, world, raw_rows0, ns0):
     return {"value": round(nbytes_total * world / (ms * 1e-3) / 1e12, 4), "unit": UNIT,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms / K, 4),
             "wall_ms_per_step": round(wall / K * 1e3, 4), "graph_captures": gs.captures,
-            "what": "per step: H2D q + new K/V token from pinned memory, a replayed CUDA graph of the "
+            "what": "per step: H2D q + new K/V token from pinned memory (read over PCIe by a copy kernel, "
+                    "exk_copy_from_host), a replayed CUDA graph of the "
                     "device-length step (append + page encode at boundaries, decode attention, length advance; "
                     "pools kept ahead with one sync per 8 pages) whose merge kernel writes the output straight "
                     "into pinned host memory over PCIe (the D2H bytes); context grows from 4096"}

@@ -68,6 +68,7 @@ _SIGNATURES.update({
                                  c_void_p, c_int64, c_void_p, c_int, c_int, c_int, c_void_p, c_int, c_void_p, c_int,
                                  c_void_p]),
     "exk_advance_length": (c_int, [c_void_p, c_int, c_int, c_void_p]),
+    "exk_copy_from_host": (c_int, [c_void_p, c_void_p, c_int64, c_int, c_void_p]),
     "exk_selftest_wait_timeout": (c_int, [c_void_p, ctypes.c_uint64, c_int, c_void_p]),
     "exk_attention_compressed_noalloc": (c_int, [c_void_p, _P(CView), _P(CView), c_int, c_int, c_int, c_int, c_int,
                                                  c_int, c_float, c_void_p, c_void_p, c_int, c_void_p]),

@@ -157,7 +157,10 @@ class CompressedKV:
         self._checked = True
         if need <= self.pool.cap:
             return False
-        self._relocate(used, need)
+        # a quarter window of slack: the next check, after `pages` pages that
+        # escaped a few per cent of their rows as usual, must not find the pool
+        # short again (each growth moves the pool and invalidates captured work)
+        self._relocate(used, need + self.headroom_rows(pages) // 4)
         return True
 
     # ------------------------------------------------------------------ filling

@@ -23,6 +23,16 @@ namespace exk {
 constexpr int kEncWarps = 8;
 constexpr int kScanThreads = 1024;
 
+// The kernels after the first of a call are programmatic dependents of the
+// kernel before them on the stream (launch_after): they may become resident
+// while it runs its last wave, which hides their launch latency, and wait in
+// after_prior() until it has completed and its writes are visible (a no-op
+// after an ordinary launch). allow_dependents() lets them be scheduled.
+__device__ __forceinline__ void after_prior() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void allow_dependents() {
+  if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 struct EncArgs {
   const uint16_t* src;
   int64_t s_b, s_pg, s_p, s_h;
@@ -136,6 +146,7 @@ __device__ __forceinline__ void load_row_quads(const uint16_t* p, int q, uint32_
 
 template <bool VEC>
 __global__ void __launch_bounds__(kEncWarps * 32, 4) encode_kernel(const __grid_constant__ EncArgs a) {
+  allow_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ph = blockIdx.x * kEncWarps + warp;
   if (ph >= a.n_ph) return;  // whole warp
@@ -249,6 +260,8 @@ __global__ void __launch_bounds__(kEncWarps * 32, 4) encode_kernel(const __grid_
 __global__ void __launch_bounds__(kScanThreads) raw_offsets_kernel(const __grid_constant__ EncArgs a) {
   __shared__ int s_warp[kScanThreads / 32];
   __shared__ int s_total;
+  allow_dependents();
+  after_prior();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   int pg0 = a.pg0;
   if (a.T_stride == 0 && !launch_page(a, 0, pg0)) return;  // one length: uniform over the CTA
@@ -306,6 +319,7 @@ __global__ void __launch_bounds__(kScanThreads) raw_offsets_kernel(const __grid_
 // source into pool row rowoff + rank; rows at or past raw_cap are skipped.
 template <bool VEC>
 __global__ void __launch_bounds__(kEncWarps * 32) raw_copy_kernel(const __grid_constant__ EncArgs a) {
+  after_prior();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ph = blockIdx.x * kEncWarps + warp;
   if (ph >= a.n_ph) return;
@@ -360,6 +374,8 @@ __device__ __forceinline__ int64_t prefill_page(const EncArgs& a, int ph) {
 
 __global__ void __launch_bounds__(kChunkThreads) chunk_sums_kernel(const __grid_constant__ EncArgs a) {
   __shared__ int s_warp[kChunkThreads / 32];
+  allow_dependents();
+  after_prior();
   const int c0 = blockIdx.x * kChunkPh;
   int n = 0;
 #pragma unroll
@@ -381,6 +397,8 @@ __global__ void __launch_bounds__(kChunkThreads) chunk_sums_kernel(const __grid_
 __global__ void __launch_bounds__(kScanThreads) chunk_scan_kernel(const __grid_constant__ EncArgs a) {
   __shared__ int s_warp[kScanThreads / 32];
   __shared__ int s_total;
+  allow_dependents();
+  after_prior();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int n_chunks = (a.n_ph + kChunkPh - 1) / kChunkPh;
   int carry = *a.cnt;
@@ -421,6 +439,7 @@ __global__ void __launch_bounds__(kChunkThreads) chunk_place_kernel(const __grid
   __shared__ uint32_t s_rm[kChunkPh];
   __shared__ int s_warp[kChunkThreads / 32];
   __shared__ int s_base;
+  after_prior();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int c0 = blockIdx.x * kChunkPh;
   constexpr int kPer = kChunkPh / kChunkThreads;
@@ -584,6 +603,28 @@ __global__ void __launch_bounds__(256) decode_kernel(const __grid_constant__ Dec
 
 using namespace exk;
 
+namespace {
+
+// Launches kern as a programmatic dependent of the kernel before it on the stream.
+int launch_after(void (*kern)(EncArgs), int grid, int block, cudaStream_t st, const EncArgs& a) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
+  if (e == cudaSuccess) return 0;
+  (void)cudaGetLastError();  // reported here, not by the next launch's check
+  return static_cast<int>(e);
+}
+
+}  // namespace
+
 extern "C" int exk_encode_pages(const uint16_t* src, int64_t s_b, int64_t s_pg, int64_t s_p, int64_t s_h,
                                 uint8_t* sm, uint8_t* code, uint8_t* base, int32_t* rowmask, int32_t* rowoff,
                                 uint16_t* raw, int64_t raw_cap, int32_t* cnt, int b0, int pg0, int nb, int npg, int H,
@@ -637,15 +678,9 @@ extern "C" int exk_encode_pages(const uint16_t* src, int64_t s_b, int64_t s_pg, 
     encode_kernel<false><<<blocks, kEncWarps * 32, 0, st>>>(a);
   if ((r = launch_status()) != 0) return r;
   const int chunks = static_cast<int>((n_ph + kChunkPh - 1) / kChunkPh);
-  chunk_sums_kernel<<<chunks, kChunkThreads, 0, st>>>(a);
-  if ((r = launch_status()) != 0) return r;
-  chunk_scan_kernel<<<1, kScanThreads, 0, st>>>(a);
-  if ((r = launch_status()) != 0) return r;
-  if (vec)
-    chunk_place_kernel<true><<<chunks, kChunkThreads, 0, st>>>(a);
-  else
-    chunk_place_kernel<false><<<chunks, kChunkThreads, 0, st>>>(a);
-  return launch_status();
+  if ((r = launch_after(chunk_sums_kernel, chunks, kChunkThreads, st, a)) != 0) return r;
+  if ((r = launch_after(chunk_scan_kernel, 1, kScanThreads, st, a)) != 0) return r;
+  return launch_after(vec ? chunk_place_kernel<true> : chunk_place_kernel<false>, chunks, kChunkThreads, st, a);
 }
 
 extern "C" int exk_decode_to_bf16(const exk_cview* c, int B, int TS, int H, int T, uint16_t* out, int32_t* status,
@@ -727,13 +762,45 @@ extern "C" int exk_append_token(const uint16_t* x, int64_t x_sb, int64_t x_sh, u
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   encode_kernel<true><<<blocks, kEncWarps * 32, 0, st>>>(a);
   if ((r = launch_status()) != 0) return r;
-  raw_offsets_kernel<<<1, kScanThreads, 0, st>>>(a);
-  if ((r = launch_status()) != 0) return r;
-  raw_copy_kernel<true><<<blocks, kEncWarps * 32, 0, st>>>(a);
-  return launch_status();
+  if ((r = launch_after(raw_offsets_kernel, 1, kScanThreads, st, a)) != 0) return r;
+  return launch_after(raw_copy_kernel<true>, blocks, kEncWarps * 32, st, a);
 }
 
 __global__ void advance_kernel(int32_t* T_dev, int n) { *T_dev += n; }
+
+// Copy from mapped pinned host memory by the SMs: 16-byte loads over PCIe,
+// kCopyIn per thread issued before any store, so a step's few hundred KB of
+// inputs cross in about one round trip.
+constexpr int kCopyIn = 4;
+
+__global__ void __launch_bounds__(256) copy_in_kernel(uint4* __restrict__ dst, const uint4* __restrict__ src, int64_t n) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * 256;
+  for (int64_t i0 = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x; i0 < n; i0 += kCopyIn * stride) {
+    uint4 v[kCopyIn];
+#pragma unroll
+    for (int j = 0; j < kCopyIn; ++j)
+      if (i0 + j * stride < n) v[j] = src[i0 + j * stride];
+#pragma unroll
+    for (int j = 0; j < kCopyIn; ++j)
+      if (i0 + j * stride < n) dst[i0 + j * stride] = v[j];
+  }
+}
+
+extern "C" int exk_copy_from_host(void* dst, const void* src, int64_t bytes, int device, void* stream) {
+  if (dst == nullptr || src == nullptr || bytes <= 0) return EXK_EARG;
+  if ((reinterpret_cast<uintptr_t>(dst) & 15u) != 0 || (reinterpret_cast<uintptr_t>(src) & 15u) != 0 ||
+      bytes % 16 != 0)
+    return EXK_EALIGN;
+  int sms = 0;
+  int r = use_device(device, &sms);
+  if (r != 0) return r;
+  if (device_reachable(src) != 0 || device_reachable(dst) != 0) return EXK_EARG;
+  const int64_t n = bytes / 16;
+  const int64_t grid = std::min<int64_t>((n + 255) / 256, 4 * static_cast<int64_t>(sms));
+  copy_in_kernel<<<static_cast<unsigned>(grid), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<uint4*>(dst), static_cast<const uint4*>(src), n);
+  return launch_status();
+}
 
 extern "C" int exk_advance_length(int32_t* T_dev, int n, int device, void* stream) {
   if (T_dev == nullptr) return EXK_EARG;

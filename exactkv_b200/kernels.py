@@ -344,6 +344,22 @@ def append_token(x, c, T_dev):
     check(rc, "exk_append_token")
 
 
+def copy_from_host(dst, src):
+    """dst (a contiguous CUDA tensor) <- src (a contiguous pinned CPU tensor of
+    the same byte size): a kernel on the current stream reads the pinned
+    memory over PCIe (exk_copy_from_host), so the copy needs no hand-off
+    between the copy engine and the step's kernels. Returns dst."""
+    if not (dst.is_cuda and dst.is_contiguous() and src.is_contiguous() and not src.is_cuda and src.is_pinned()):
+        raise ValueError("dst must be a contiguous CUDA tensor and src a contiguous pinned host tensor")
+    n = dst.numel() * dst.element_size()
+    if src.numel() * src.element_size() != n:
+        raise ValueError("dst and src must hold the same number of bytes")
+    dev = dst.device
+    check(lib.exk_copy_from_host(dst.data_ptr(), src.data_ptr(), n, dev.index,
+                                 torch.cuda.current_stream(dev).cuda_stream), "exk_copy_from_host")
+    return dst
+
+
 def advance_length(T_dev, n=1):
     dev = T_dev.device
     check(lib.exk_advance_length(T_dev.data_ptr(), n, dev.index, torch.cuda.current_stream(dev).cuda_stream),

@@ -272,6 +272,15 @@ int exk_selftest_wait_timeout(int32_t *status, uint64_t limit_ns, int device, vo
 /* *T_dev += n on `stream` (the end of a device-length decode step). */
 int exk_advance_length(int32_t *T_dev, int n, int device, void *stream);
 
+/* Copies `bytes` (a multiple of 16; both addresses 16-byte aligned) from
+ * page-locked host memory mapped into the device's address space (as
+ * cudaHostAlloc gives it) into device memory, by a kernel on `stream` rather
+ * than a copy-engine transfer: a decode step's inputs then reach the device
+ * with no hand-off between the copy engine and the kernels before and after
+ * them. EXK_EARG when either address is not reachable from the device. No
+ * counterpart in the reference. */
+int exk_copy_from_host(void *dst, const void *src, int64_t bytes, int device, void *stream);
+
 /* Decode attention over paged caches: the cache buffers `k`, `v` are a pool of
  * pool_pages 16-token pages (sm [pool_pages * 16, Hkv, 128], code, base
  * [pool_pages, Hkv, 128], rowmask/rowoff [pool_pages, Hkv], raw as usual — any

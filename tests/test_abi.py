@@ -109,6 +109,10 @@ def test_entry_points_reject_bad_arguments_before_any_launch():
     assert lib.exk_attn_merge_peers(flags, 2, 2, counts, 1, 32, dev_addr, flags, 1, dev_addr, None, 0, None) == EARG
     assert lib.exk_attn_merge_partial(ctypes.byref(ws), 32, 3, 3, dev_addr, dev_addr, dev_addr, 0, None) == EARG
     assert lib.exk_attn_merge_partial(ctypes.byref(ws), 32, 0, 5, dev_addr, dev_addr, dev_addr, 0, None) == EARG
+    assert lib.exk_copy_from_host(dev_addr, dev_addr, 0, 0, None) == EARG           # nothing to copy
+    assert lib.exk_copy_from_host(None, dev_addr, 64, 0, None) == EARG
+    assert lib.exk_copy_from_host(dev_addr, dev_addr + 8, 64, 0, None) == EALIGN    # source not 16-byte aligned
+    assert lib.exk_copy_from_host(dev_addr, dev_addr, 24, 0, None) == EALIGN        # not whole 16-byte words
     for code in (EARG, EALIGN, -3, -4, EHEADS, -6):
         assert lib.exk_error_string(code).startswith(b"exactkv_b200:")
     assert b"peer" in lib.exk_status_string(6)

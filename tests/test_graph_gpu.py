@@ -130,3 +130,24 @@ def test_output_to_pinned_host_memory():
     with pytest.raises(ValueError):
         kernels.attention_compressed_devlen(q, kc, vc, lens, 0, out=torch.empty(B, Hq, 128, dtype=torch.bfloat16))
     kernels.check_status()
+
+
+@pytest.mark.parametrize("nbytes", [16, 393216, 5 * 2 ** 20 + 16])
+def test_copy_from_host(nbytes):
+    """kernels.copy_from_host: a kernel copies pinned host memory into device
+    memory (one grid-stride pass of 16-byte loads, several in flight per thread
+    for large copies), byte for byte; pageable host memory is refused before any
+    launch."""
+    import ctypes
+    from exactkv_b200._lib import lib
+    g = torch.Generator().manual_seed(nbytes)
+    src = torch.randint(-2 ** 31, 2 ** 31 - 1, (nbytes // 4,), generator=g, dtype=torch.int32).pin_memory()
+    dst = torch.zeros(nbytes // 4, dtype=torch.int32, device="cuda")
+    kernels.copy_from_host(dst, src)
+    torch.cuda.synchronize()
+    assert torch.equal(dst.cpu(), src)
+    pageable = torch.zeros(64, dtype=torch.int32)
+    assert lib.exk_copy_from_host(dst.data_ptr(), pageable.data_ptr(), 256, 0, None) == -1
+    with pytest.raises(ValueError):
+        kernels.copy_from_host(dst[:64], pageable)
+    kernels.check_status()
