@@ -92,10 +92,11 @@ __device__ __forceinline__ int64_t page_index(const EncArgs& a, int pg0, int ph,
   return (static_cast<int64_t>(a.b0 + bi) * a.NP + pg0 + pg) * a.H + hk;
 }
 
-// Constants the compiler cannot see (2^25, 2^24, 1), so that the shifts and one
-// add of the encoder's second pass become multiplies on the FMA pipe: that
-// pass keeps the ALU pipe busy.
-static __constant__ uint32_t c_fma[3] = {1u << 25, 1u << 24, 1u};
+// Constants the compiler cannot see (2^25, 2^24, 1, 2), so that shifts and
+// lane-wise adds of the encoder become multiplies on the FMA pipe: the encoder
+// keeps the ALU pipe busy. A lane-wise add is a plain 32-bit add when neither
+// 16-bit lane can carry into the next: the lanes then hold 0x8000 + e - b.
+static __constant__ uint32_t c_fma[5] = {1u << 25, 1u << 24, 1u, 2u, 16u};
 
 __device__ __forceinline__ uint32_t mulhi(uint32_t x, uint32_t k) {
   uint32_t d;
@@ -170,7 +171,11 @@ __global__ void __launch_bounds__(kEncWarps * 32, 4) encode_kernel(const __grid_
   // Both passes work on two values at once in 16-bit lanes (exponents are 8
   // bits, codes and their differences fit a signed 16-bit lane).
   const uint16_t* rows = a.src + bi * a.s_b + pg * a.s_pg + static_cast<int64_t>(th * 8) * a.s_p + hk * a.s_h;
-  // pass 1: per-channel maximum and minimum exponent over the 16 tokens
+  // pass 1: per-channel maximum and minimum exponent over the 16 tokens. Each
+  // lane doubled (w * 2: the sign leaves its lane, the exponent fills the
+  // lane's high byte) orders the values by exponent first, so the lane-wise
+  // maximum and minimum carry the extreme exponents in their high bytes.
+  const uint32_t k25 = c_fma[0], k24 = c_fma[1], k1 = c_fma[2], k2 = c_fma[3], k16 = c_fma[4];
   uint32_t emax2[4], emin2[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
@@ -183,7 +188,7 @@ __global__ void __launch_bounds__(kEncWarps * 32, 4) encode_kernel(const __grid_
     load_row_quads<VEC>(rows + static_cast<int64_t>(i) * a.s_p, q, w);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const uint32_t e2 = w[j] & 0x7F807F80u;  // exponents, 7 bits up in their lanes
+      const uint32_t e2 = mad_lo(w[j], k2, 0u);
       emax2[j] = max_u16x2(emax2[j], e2);
       emin2[j] = min_u16x2(emin2[j], e2);
     }
@@ -196,16 +201,19 @@ __global__ void __launch_bounds__(kEncWarps * 32, 4) encode_kernel(const __grid_
 
   // per channel, two channels per word in 16-bit lanes: base b = max(emax - 15,
   // 0); zero group zm = (a zero exponent and b > 0); the base byte min(b + 128
-  // zm, 255); and for pass 2, -b and -(b + zm)
-  uint32_t byte2[4], nb2[4], nbz2[4], escany = 0u;
+  // zm, 255); and for pass 2 the lane biases 0x8000 - b (channels 0-63), 0x8000
+  // - 16 b (channels 64-127, whose codes go to the high nibble: 16 e is added)
+  // and 0x8000 - (b + zm) (b + zm <= 241: every biased sum stays in its lane)
+  uint32_t byte2[4], cb2[4], czb2[4], escany = 0u;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    const uint32_t e2 = emax2[j] >> 7;                                   // lanes: emax
+    const uint32_t e2 = (emax2[j] >> 8) & 0x00FF00FFu;                  // lanes: emax
+    const uint32_t z2 = (emin2[j] >> 8) & 0x00FF00FFu;                  // lanes: emin
     const uint32_t b2 = max_s16x2(add_u16x2(e2, 0xFFF1FFF1u), 0u);      // max(emax - 15, 0)
-    const uint32_t zm2 = (min_u16x2(emin2[j], 0x00010001u) ^ 0x00010001u) & min_u16x2(b2, 0x00010001u);
+    const uint32_t zm2 = (min_u16x2(z2, 0x00010001u) ^ 0x00010001u) & min_u16x2(b2, 0x00010001u);
     byte2[j] = min_u16x2(add_u16x2(b2, zm2 << 7), 0x00FF00FFu);
-    nb2[j] = add_u16x2(~b2, 0x00010001u);
-    nbz2[j] = add_u16x2(~add_u16x2(b2, zm2), 0x00010001u);
+    cb2[j] = 0x80008000u - (j < 2 ? b2 : b2 << 4);
+    czb2[j] = 0x80008000u - (b2 + zm2);
     escany |= b2 & 0xFF80FF80u;                                         // b >= 128: every row escapes
   }
   const uint32_t bw[2] = {prmt(byte2[0], byte2[1], 0x6420u), prmt(byte2[2], byte2[3], 0x6420u)};
@@ -214,8 +222,7 @@ __global__ void __launch_bounds__(kEncWarps * 32, 4) encode_kernel(const __grid_
   // pass 2: codes, sign|mantissa bytes and escapes, row by row. Per value:
   // code = max(e - b, 0) (a zero of a zero group gets 0); it escapes when
   // e != 0 and e < b + zm, or when b >= 128.
-  uint32_t escrow = escall ? 0xFFu : 0u;
-  const uint32_t k25 = c_fma[0], k24 = c_fma[1], k1 = c_fma[2];
+  uint32_t escw = escall ? 0x00FF00FFu : 0u;  // bit i / 16 + i: row i escapes in the low / high lane
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int tok = th * 8 + i;
@@ -226,32 +233,29 @@ __global__ void __launch_bounds__(kEncWarps * 32, 4) encode_kernel(const __grid_
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const uint32_t e2 = mulhi(w[j], k25) & 0x00FF00FFu;  // (w >> 7): exponents in the low byte of each lane
-      code2[j] = max_s16x2(add_u16x2(e2, nb2[j]), 0u);
-      // lane bit 15: e < b + zm; e2 + 0x7FFF: lane bit 15 iff e != 0
-      escacc |= add_u16x2(e2, nbz2[j]) & mad_lo(e2, k1, 0x7FFF7FFFu);
+      // lanes 0x8000 + max(e - b, 0) (x 16 for channels 64-127): the code in the low byte
+      code2[j] = max_u16x2(mad_lo(e2, j < 2 ? k1 : k16, cb2[j]), 0x80008000u);
+      // lane bit 15 of e2 + 0x8000 - (b + zm): e >= b + zm; of e2 + 0x7FFF: e != 0
+      escacc |= ~mad_lo(e2, k1, czb2[j]) & mad_lo(e2, k1, 0x7FFF7FFFu);
       // bit 7 of each lane's low byte from the sign (w >> 8), bits 0-6 the
       // mantissa; the high bytes are not used
       x[j] = (mulhi(w[j], k24) & 0x00800080u) | (w[j] & 0xFF7FFF7Fu);
     }
     const uint32_t smw0 = prmt(x[0], x[1], 0x6420u), smw1 = prmt(x[2], x[3], 0x6420u);
-    const uint32_t cw = prmt(code2[0], code2[1], 0x6420u) | (prmt(code2[2], code2[3], 0x6420u) << 4);
+    const uint32_t cw = prmt(code2[0] | code2[2], code2[1] | code2[3], 0x6420u);
     *reinterpret_cast<uint32_t*>(a.sm + row * kD + 4 * q) = smw0;
     *reinterpret_cast<uint32_t*>(a.sm + row * kD + 64 + 4 * q) = smw1;
     *reinterpret_cast<uint32_t*>(a.code + row * (kD / 2) + 4 * q) = cw;
-    escrow |= ((escacc & 0x80008000u) != 0u ? 1u : 0u) << i;
+    escw |= (escacc >> (15 - i)) & (0x00010001u << i);
   }
   if (th == 0) {
     *reinterpret_cast<uint32_t*>(a.base + page * kD + 4 * q) = bw[0];
     *reinterpret_cast<uint32_t*>(a.base + page * kD + 64 + 4 * q) = bw[1];
   }
-  // rowmask: token 8th+i escapes if any of its 16 lanes saw an escape
-  uint32_t rm = 0;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const uint32_t bal = __ballot_sync(0xFFFFFFFFu, (escrow >> i) & 1u);
-    rm |= ((bal & 0xFFFFu) ? 1u : 0u) << i;
-    rm |= ((bal >> 16) ? 1u : 0u) << (8 + i);
-  }
+  // rowmask: token 8th+i escapes if any of its 16 lanes saw an escape (bit i
+  // of escrow in lanes 16th..16th+15: bit 8th+i of one warp-wide OR)
+  const uint32_t escrow = (escw | (escw >> 16)) & 0xFFu;
+  const uint32_t rm = __reduce_or_sync(0xFFFFFFFFu, escrow << (8 * th));
   if (lane == 0) a.rowmask[page] = static_cast<int32_t>(rm);
 }
 
