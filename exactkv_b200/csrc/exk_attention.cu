@@ -190,12 +190,20 @@ __device__ __forceinline__ Item decode_item(const AttnArgs& a, int item) {
       Su = max(1, ((T + kP - 1) / kP + WPH - 1) / WPH);
       W = static_cast<int64_t>(a.B) * a.ngroups * Su;
     }
-    const int64_t c = item % G, j = item / G;
-    const int64_t lo = c * W / G, hi = (c + 1) * W / G;
-    const int64_t u = lo / Su + j;
+    // Quotients of products below 2^41 (W < 2^31 stages, G <= 1024 CTAs) in
+    // double precision: the products are exact and the division is correctly
+    // rounded; a non-integer c W / G lies at least 1/G from an integer and is
+    // rounded by less than 2^-22, a non-integer (x + 1) G / W at least 1/W and
+    // by less than 2^-42, so floor and ceil come out exact. (64-bit integer
+    // divisions here cost ~1 us at every item start.)
+    const int c = item % a.bal_G, j = item / a.bal_G;
+    const double dW = static_cast<double>(W), dG = static_cast<double>(G);
+    const int64_t lo = static_cast<int64_t>(static_cast<double>(c) * dW / dG);
+    const int64_t hi = static_cast<int64_t>(static_cast<double>(c + 1) * dW / dG);
+    const int64_t u = static_cast<int>(lo) / static_cast<int>(Su) + j;
     const int64_t s0 = max(lo, u * Su), s1 = min(hi, (u + 1) * Su);
-    it.b = static_cast<int>(u / a.ngroups);
-    it.hg = static_cast<int>(u % a.ngroups);
+    it.b = static_cast<int>(u) / a.ngroups;
+    it.hg = static_cast<int>(u) % a.ngroups;
     if (s0 >= s1 || u * Su >= W) {  // past this CTA's run: no pages, no partial
       it.b = it.hg = 0;              // (u may lie past the last unit)
       it.split = -1;
@@ -204,7 +212,7 @@ __device__ __forceinline__ Item decode_item(const AttnArgs& a, int item) {
       return it;
     }
     // the CTA whose run holds stage x (runs are empty where there are fewer stages than CTAs)
-    auto owner = [&](int64_t x) { return ((x + 1) * G + W - 1) / W - 1; };
+    auto owner = [&](int64_t x) { return static_cast<int64_t>(ceil(static_cast<double>(x + 1) * dG / dW)) - 1; };
     const int64_t first = owner(u * Su);
     it.split = static_cast<int>(c - first);
     // the piece closes the columns of the empty runs up to the unit's next
@@ -1570,7 +1578,10 @@ extern "C" int exk_plan_splits(int B, int Hkv, int T, int num_ctas, int32_t* ns_
 
 namespace {
 
-// The balanced partition of a launch: units of Su stages, cut into G equal runs.
+// The balanced partition of a launch: units of Su stages, cut into G equal runs
+// (W = units * Su < 2^31 stages and G <= kMaxBalancedCtas, which keep the
+// kernel's double-precision quotients exact).
+constexpr int64_t kMaxBalancedCtas = 1024;
 struct Balance {
   int64_t units, Su, W, G;
   int splits;    // most pieces one unit is cut into (the workspace columns needed)
@@ -1609,6 +1620,8 @@ int balance_args(AttnArgs& a, const exk_partials* ws, int hg, int wph, int sms) 
     const int64_t units = static_cast<int64_t>(a.B) * (a.Hkv / hg);
     const int64_t G = sms;
     const int64_t splits = (G + units - 1) / units + 1, pieces = (units + G - 1) / G + 1;
+    const int64_t w_cap = units * ((((a.T + kP - 1) / kP) + wph - 1) / wph);
+    if (w_cap >= (int64_t{1} << 31) || G > kMaxBalancedCtas) return EXK_EARG;
     if (splits > ws->ns) return EXK_EARG;
     if (G * pieces > (int64_t{1} << 30)) return EXK_EARG;
     a.bal_G = static_cast<int>(G);
@@ -1618,6 +1631,7 @@ int balance_args(AttnArgs& a, const exk_partials* ws, int hg, int wph, int sms) 
     return 0;
   }
   const Balance b = balance_of(a.B, a.Hkv / hg, a.T, wph, sms);
+  if (b.W >= (int64_t{1} << 31) || b.G > kMaxBalancedCtas) return EXK_EARG;
   if (b.splits > ws->ns) return EXK_EARG;  // the workspace must hold every piece of a unit
   if (b.G * b.pieces > (int64_t{1} << 30)) return EXK_EARG;
   a.bal_G = static_cast<int>(b.G);
@@ -1645,7 +1659,8 @@ extern "C" int exk_plan_balanced(int B, int Hkv, int T, int num_ctas, int consum
   // any_length: the call reads one batch-wide length on the device (at most T):
   // the workspace bound that holds for every length
   const int64_t splits = any_length ? (b.G + b.units - 1) / b.units + 1 : b.splits;
-  *ns_out = (bal_cost < uni_cost && splits <= 4096) ? static_cast<int32_t>(splits) : 0;
+  const bool fits = b.W < (int64_t{1} << 31) && b.G <= kMaxBalancedCtas;  // the kernel's exact quotients
+  *ns_out = (fits && bal_cost < uni_cost && splits <= 4096) ? static_cast<int32_t>(splits) : 0;
   return 0;
 }
 

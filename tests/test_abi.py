@@ -167,3 +167,22 @@ def test_balanced_plan_host_side():
     assert lib.exk_plan_balanced(1, 4, 32768, 148, 8, 1, ctypes.byref(ns)) == 0 and ns.value == 0
     assert lib.exk_plan_balanced(0, 8, 4096, 148, 8, 0, ctypes.byref(ns)) == -1
     assert lib.exk_plan_balanced(32, 8, 4096, 148, 6, 0, ctypes.byref(ns)) == -1
+
+
+def test_balanced_plan_quotients_are_exact_in_double():
+    """The attention kernel computes the balanced plan's run bounds floor(c W / G)
+    and owners ceil((x + 1) G / W) - 1 with IEEE double division (W < 2^31
+    stages, G <= 1024 CTAs): they equal the integer formulas, also next to the
+    limits."""
+    import numpy as np
+    rng = np.random.default_rng(5)
+    Ws = np.concatenate([rng.integers(1, 2 ** 31, 4000), [2 ** 31 - 1, 2 ** 31 - 2, 1, 2, 147, 148, 149]])
+    for W in Ws.tolist():
+        for G in (148, 1024, 1023, 7):
+            cs = np.unique(np.concatenate([rng.integers(0, G + 1, 16), [0, 1, G - 1, G]]))
+            for c in cs.tolist():
+                assert int(c * W / G) == (c * W) // G
+            xs = np.unique(np.concatenate([rng.integers(0, W, 16), [0, W - 1]]))
+            for x in xs.tolist():
+                import math
+                assert math.ceil((x + 1) * G / W) - 1 == ((x + 1) * G + W - 1) // W - 1
