@@ -1609,7 +1609,8 @@ Balance balance_of(int B, int ngroups, int T, int wph, int ctas) {
 }
 
 // Fills the balanced partition of a whole-call launch (ws->split_len == 0):
-// host lengths and contiguous caches only; the grid is then exactly bal_G.
+// contiguous caches, a host-side length or one device-side length for the
+// batch; the grid is then exactly bal_G.
 int balance_args(AttnArgs& a, const exk_partials* ws, int hg, int wph, int sms) {
   if (ws->split_len != 0) return 0;
   if (a.pages != nullptr || (a.T_dev != nullptr && a.T_stride != 0)) return EXK_EARG;
